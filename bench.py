@@ -1,0 +1,383 @@
+"""Benchmark of the B200 path on BASELINE.json's metric.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (the metric's configs[1]): the fused map
+y = sin(x^2+3x) plus its calculus-pass derivative dy = cos(x^2+3x)(2x+3),
+f32, 2^28 elements per GPU (weak scaling: each rank owns a contiguous 2^28
+element shard of an N*2^28 element problem; no data-path collective). One
+step = one pass of the hot path over one shard; value = whole-job HBM GB/s
+at 12 algorithmic bytes per element. The other BASELINE configs (1, 3, 4,
+4', 5) are measured the same way and reported under "configs".
+
+Timing: W warm-up steps, then K steps bracketed by a barrier and a device
+synchronise, CUDA events on the launching stream, max over ranks. Inputs
+(1 GiB per shard) exceed the 126 MB L2, so no flush is needed. nvidia-smi
+clocks are sampled during the timed region. `e2e` is the same metric through
+the C-ABI host entry (mlkb_module_run_host) from pinned host buffers, with
+the H2D copy of x and the D2H copy of y and dy inside every step.
+
+--impl reference times the reference's own CPU executor (oracle/_ref, built
+from the reference sources; the C restatement when absent) on rank 0 with
+all host threads, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SEED = 0x4D4C4B2B
+BYTES_PER_ELEM_MAP2 = 12  # x read + y, dy written (f32)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def load_traffic():
+    """Per-launch DRAM traffic of each config's dominant kernel, from the
+    committed ncu summaries (profiles/traffic.json), if captured."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (every 200 ms)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def cpu_reference_map2(n_sample: int, steps: int):
+    """The reference's own executor (or the C port) on a bounded sample of
+    the config-2 workload, all host threads. Returns (GB/s, kind, cores, secs)."""
+    import numpy as np
+
+    import oracle
+    from mlk2_b200 import kir
+
+    cores = os.cpu_count() or 1
+    x = oracle.fill_uniform_f32(n_sample, SEED, 2, -8.0, 8.0).astype(np.float64)
+    chains = [kir.SIN_CHAIN, kir.DSIN_CHAIN]
+    if oracle.ref_available():
+        ex, kind = oracle.ref(), "reference"
+        run = lambda: ex.chain(chains, x, threads=cores)  # noqa: E731
+    else:
+        ex, kind, cores = oracle.port(), "port", 1
+        run = lambda: ex.chain(chains, x)  # noqa: E731
+    run()
+    times = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return n_sample * BYTES_PER_ELEM_MAP2 / t / 1e9, kind, cores, t
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return
+    n_sample = 1 << 24
+    value, kind, cores, t = cpu_reference_map2(n_sample, args.steps)
+    line = {
+        "metric": "HBM GB/s (map/softmax) & GEMM TFLOP/s vs B200 peak at 1/2/4/8 GPUs",
+        "impl": "reference", "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic",
+        "config": {"workload": "config2: y=sin(x^2+3x), dy=cos(x^2+3x)(2x+3), f32 inputs, "
+                               f"sample {n_sample} elements per step (of 2^28)",
+                   "elements_per_step": n_sample},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": f"{n_sample} elements of config 2 per step, f64 arithmetic, "
+                                   "bytes counted at f32 width (12 B/element)"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def time_device(torch, fn, warmup, steps, dist, world):
+    """W untimed steps, then K steps between barrier+sync; CUDA events on the
+    current stream; max over ranks. Returns seconds per step."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms / 1e3
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--headline-only", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import mlk2_b200 as mb
+    from mlk2_b200 import api, kir
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    peaks = load_peaks()
+    traffic = load_traffic()
+
+    # ---- headline: config 2, map + derivative, 2^28 f32 per GPU ----------------
+    n = 1 << 28
+    x = torch.empty(n, dtype=torch.float32, device="cuda")
+    api.fill(x, SEED, 2 + 256 * rank, "uniform", -8.0, 8.0)
+    y = torch.empty_like(x)
+    dy = torch.empty_like(x)
+    step = lambda: api.map_sin_dsin(x, y, dy)  # noqa: E731
+    with ClockSampler(local) as clk:
+        sec = time_device(torch, step, args.warmup, args.steps, dist, world)
+    clocks = clk.summary()
+    alg_bytes = n * BYTES_PER_ELEM_MAP2
+    achieved = alg_bytes / sec / 1e9
+    value = world * alg_bytes / sec / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                "kernel": "map_vec_kernel<SinDsinOp>",
+                "traffic": traffic.get("map2", {}).get("bytes_per_launch")}
+
+    # ---- e2e through the C-ABI host entry ---------------------------------------
+    del y, dy
+    xh = torch.empty(n, dtype=torch.float32).pin_memory()
+    yh = torch.empty(n, dtype=torch.float32).pin_memory()
+    dyh = torch.empty(n, dtype=torch.float32).pin_memory()
+    xh.copy_(x.cpu())
+    del x
+    torch.cuda.empty_cache()
+    module = api.Module(kir.map_module([kir.SIN_CHAIN, kir.DSIN_CHAIN]))
+    bufs = [xh, yh, dyh]
+    module.run_host(bufs, n=n, n_gpus=1)  # warm the device buffer cache
+    e2e_steps = max(2, min(args.steps, 5))
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        module.run_host(bufs, n=n, n_gpus=1)
+    e2e_sec = (time.perf_counter() - t0) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_sec], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_sec = float(t.item())
+    e2e = {"value": world * alg_bytes / e2e_sec / 1e9, "unit": "GB/s",
+           "h2d_bytes_per_step": n * 4, "d2h_bytes_per_step": n * 8,
+           "ms_per_step": e2e_sec * 1e3, "api": "mlkb_module_run_host (pinned host f32)"}
+    del xh, yh, dyh, bufs, module
+    torch.cuda.empty_cache()
+
+    # ---- the other BASELINE configs ---------------------------------------------
+    configs = {}
+    if not args.headline_only:
+        configs = other_configs(torch, api, args, dist, world, rank, peaks, traffic)
+
+    # ---- CPU baseline (rank 0, N = 1 only) ----------------------------------------
+    cpu = None
+    if rank == 0 and world == 1:
+        v, kind, cores, t = cpu_reference_map2(1 << 24, 3)
+        cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind,
+               "sample": "2^24 elements of config 2 per run (median of 3), f64 arithmetic, "
+                         "bytes counted at f32 width (12 B/element)"}
+
+    if rank == 0:
+        line = {
+            "metric": "HBM GB/s (map/softmax) & GEMM TFLOP/s vs B200 peak at 1/2/4/8 GPUs",
+            "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded SplitMix64 U(-8,8), generated on the device)",
+            "config": {"workload": "config2: y=sin(x^2+3x) and dy/dx=cos(x^2+3x)(2x+3), one "
+                                   "fused kernel, f32 in/out, f64 arithmetic",
+                       "elements_per_gpu": n, "global_elements": n * world,
+                       "parallelism": f"dp{world} (contiguous element shards)",
+                       "l2": "inputs 1 GiB per GPU > 126 MB L2, no flush"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": args.steps + sum(c.get("gpu_launches", 0) for c in configs.values()),
+            "clocks": clocks, "configs": configs, "library": mb.version(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
+    out = {}
+    steps, warm = args.steps, args.warmup
+
+    def rec(name, sec, work, unit, bound, peak, launches, extra=None):
+        achieved = work / sec / (1e9 if unit == "GB/s" else 1e12)
+        d = {"value": world * achieved, "unit": unit, "ms_per_step": sec * 1e3,
+             "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                          "frac": achieved / peak,
+                          "traffic": traffic.get(name, {}).get("bytes_per_launch")},
+             "gpu_launches": launches * steps}
+        if extra:
+            d.update(extra)
+        out[name] = d
+
+    # config 1: y = sin(x^2+3x), 2^24 f32 (64 MiB in: L2 flushed between steps)
+    n1 = 1 << 24
+    x = torch.empty(n1, device="cuda")
+    api.fill(x, SEED, 1 + 256 * rank, "uniform", -4.0, 4.0)
+    y = torch.empty_like(x)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def step1():
+        flush.zero_()
+        api.map_sin(x, y)
+    t_flush = time_device(torch, flush.zero_, warm, steps, dist, world)
+    sec = time_device(torch, step1, warm, steps, dist, world) - t_flush
+    rec("map1", sec, n1 * 8, "GB/s", "hbm", peaks["hbm_gbs"], 1,
+        {"note": "L2 flushed by a 256 MiB memset before each step; its time subtracted"})
+    del x, y
+
+    # config 3: softmax [65536 x 4096] f32 per GPU
+    xs = torch.empty((65536, 4096), device="cuda")
+    api.fill(xs, SEED, 3 + 256 * rank, "normal", 0.0, 4.0)
+    ys = torch.empty_like(xs)
+    sec = time_device(torch, lambda: api.softmax(xs, ys), warm, steps, dist, world)
+    rec("softmax", sec, 2 * 4 * 65536 * 4096, "GB/s", "hbm", peaks["hbm_gbs"], 1)
+    del xs, ys
+
+    # config 4: GEMM 8192^3 f16 -> f32 (M-block shard per GPU in weak scaling)
+    n4 = 8192
+    a = torch.empty((n4, n4), dtype=torch.float16, device="cuda")
+    b = torch.empty((n4, n4), dtype=torch.float16, device="cuda")
+    api.fill(a, SEED, 41 + 256 * rank, "normal", 0.0, n4 ** -0.5)
+    api.fill(b, SEED, 42, "normal", 0.0, n4 ** -0.5)
+    c = torch.empty((n4, n4), device="cuda")
+    sec = time_device(torch, lambda: api.gemm(a, b, c), warm, steps, dist, world)
+    rec("gemm_f16", sec, 2.0 * n4 ** 3, "TFLOP/s", "tensor", peaks["bf16_tflops"], 1,
+        {"peak_note": "peak = measured cuBLAS bf16 dense burst (f16 has the same rate)"})
+    del a, b, c
+
+    # config 4': GEMM 1024^3 f32 (SIMT FMA)
+    a = torch.randn((1024, 1024), device="cuda") / 32
+    b = torch.randn((1024, 1024), device="cuda") / 32
+    c = torch.empty((1024, 1024), device="cuda")
+    sec = time_device(torch, lambda: api.gemm(a, b, c), warm, steps, dist, world)
+    rec("gemm_f32_1024", sec, 2.0 * 1024 ** 3, "TFLOP/s", "fp32-simt", 80.0, 1,
+        {"peak_note": "nominal FP32 SIMT 80 TFLOP/s (context only)"})
+    del a, b, c
+
+    # config 5: batched Q K^T * s + softmax, 256 x [2048 x 2048], d = 128
+    bq, s, d = 256, 2048, 128
+    q = torch.empty((bq, s, d), dtype=torch.float16, device="cuda")
+    k = torch.empty((bq, s, d), dtype=torch.float16, device="cuda")
+    api.fill(q, SEED, 51 + 256 * rank, "normal", 0.0, 1.0)
+    api.fill(k, SEED, 52 + 256 * rank, "normal", 0.0, 1.0)
+    yq = torch.empty((bq, s, s), device="cuda")
+    sec = time_device(torch, lambda: api.qk_softmax(q, k, yq, d ** -0.5), warm, steps, dist, world)
+    alg = 2 * bq * s * d * 2 + bq * s * s * 4
+    rec("qk_softmax", sec, alg, "GB/s", "hbm", peaks["hbm_gbs"], 2,
+        {"tflops": 2.0 * bq * s * s * d / sec / 1e12})
+    del q, k, yq
+    torch.cuda.empty_cache()
+    return out
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,257 @@
+/*
+ * mlkb200 — B200 (sm_100a) execution path for MLK+ Kernel IR modules.
+ *
+ * C ABI of libmlkb200.so. Plain pointers and sizes only; no torch or CUDA
+ * types appear in any signature (streams are passed as `void*`, i.e. a
+ * cudaStream_t, NULL = the legacy default stream of the current device).
+ *
+ * Three layers, top to bottom:
+ *   1. The reference artifact ABI (`mlk_kernel`, `mlk_bind_module`,
+ *      `mlk_last_status`): what MLK+'s backend driver dlsym()s and calls
+ *      through LoadedKernel::run with host f64 buffers.
+ *   2. Module entry points (`mlkb_module_*`): a Kernel IR module in the
+ *      reference's `mlk-kernel` JSON wire format, run over typed device or
+ *      host buffers (f16 / f32 / f64), optionally sharded over GPUs.
+ *   3. Direct kernel entry points (`mlkb_map_*`, `mlkb_softmax_*`,
+ *      `mlkb_gemm_*`, `mlkb_qk_softmax_*`) over device pointers on a stream.
+ *
+ * Every entry point returns an mlkb status (0 = ok). Codes 1-4 keep the
+ * meaning the reference artifact ABI gives them
+ * (reference docs/kernel_abi.md:36-41, backends/cpu/src/cuda_emitter.cpp:1912-1913);
+ * 5-9 are new. A human-readable message for the last failure on the calling
+ * thread is returned by mlkb_last_error().
+ */
+#ifndef MLKB200_H
+#define MLKB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define MLKB_OK 0
+#define MLKB_ERR_NEG_STORE 1   /* negative store flat index (reference code 1) */
+#define MLKB_ERR_CUDA_MEM 2    /* CUDA allocation or copy failed (reference code 2) */
+#define MLKB_ERR_LAUNCH 3      /* kernel launch or synchronisation failed (reference code 3) */
+#define MLKB_ERR_NO_DEVICE 4   /* no CUDA device (reference code 4) */
+#define MLKB_ERR_NCCL 5        /* collective failure */
+#define MLKB_ERR_TIMEOUT 6     /* a bounded device-side wait gave up */
+#define MLKB_ERR_UNSUPPORTED 7 /* module shape not recognised by this path */
+#define MLKB_ERR_INVALID 8     /* bad argument, shape, dtype or alignment */
+#define MLKB_ERR_NOT_BOUND 9   /* mlk_kernel called with no module bound */
+
+/* ---- element types ----------------------------------------------------- */
+#define MLKB_F16 1
+#define MLKB_F32 2
+#define MLKB_F64 3
+
+/* ---- module classes (what the pattern matcher recognised) --------------- */
+#define MLKB_KIND_MAP 1        /* one or more 1-D Loop{Compute;Store} roots */
+#define MLKB_KIND_SOFTMAX 2    /* Call(Softmax) */
+#define MLKB_KIND_MATMUL 3     /* Call(MatMul) */
+#define MLKB_KIND_REDUCESUM 4  /* Call(ReduceSum) */
+#define MLKB_KIND_QK_SOFTMAX 5 /* Call(MatMul) -> scale map -> Call(Softmax) */
+
+/*
+ * One expression of a fused per-element chain: the reference's KernelExpr
+ * (compiler/include/mlk/support/kernel_ir.h:89-97) with its two operands
+ * (KernelOperand, kernel_ir.h:58-83) flattened.
+ *   op      mlk::MathOp numbering (compiler/include/mlk/ir/math_op.h:18-36):
+ *           Add=0 Sub=1 Mul=2 Div=3 Neg=4 Pow=5 Exp=6 Log=7 Sin=8 Cos=9
+ *           Tan=10 Tanh=11 Sqrt=12 Rsqrt=13 Erf=14 Gelu=15
+ *   *_kind  KernelOperand::Kind numbering: Const=0 ElemA=1 ElemB=2
+ *           ScalarParam=3 Temp=4 (ElemIdx=5 is multi-dim only, not accepted)
+ *   *_index ScalarParam: scalar slot; Temp: index of an earlier expression
+ *   *_value Const payload
+ */
+typedef struct mlkb_expr {
+    int32_t op;
+    int32_t a_kind;
+    int64_t a_index;
+    double a_value;
+    int32_t b_kind;
+    int32_t reserved;
+    int64_t b_index;
+    double b_value;
+} mlkb_expr;
+
+typedef struct mlkb_module mlkb_module; /* opaque bound Kernel IR module */
+
+/* ======================================================================= */
+/* 1. Reference artifact ABI                                                */
+/* ======================================================================= */
+
+/*
+ * Binds the module that subsequent mlk_kernel calls execute, given in the
+ * reference's `mlk-kernel` JSON format (the output of KernelModule::toJson,
+ * reference compiler/src/support/kernel_ir.cpp:97-254). Replaces the module
+ * knowledge the reference bakes into each emitted artifact
+ * (reference backends/cpu/src/cuda_emitter.cpp:1563-1937). Passing NULL
+ * unbinds. When nothing is bound, mlk_kernel reads `module.json` from the
+ * directory holding this library (the fastkernel artifact-cache layout,
+ * reference fastkernel/src/fast_kernel.cpp:811-845).
+ */
+int mlk_bind_module(const char* mlk_kernel_json);
+
+/*
+ * The artifact entry point resolved by dlsym(handle, "mlk_kernel")
+ * (reference backends/cpu/src/backend_driver.cpp:418-436) and invoked by
+ * LoadedKernel::run (backend_driver.cpp:821-1050) in one of two forms:
+ *   multi-dim:  int  mlk_kernel(const double* B0, const int64_t* B0_dims, ...,
+ *                               const double* mlk_scalars, int64_t mlk_n_scalars)
+ *   legacy 1-D: void mlk_kernel(const double* B0, ..., int64_t n,
+ *                               const double* mlk_scalars, int64_t mlk_n_scalars)
+ * (reference backends/cpu/include/mlk/backend/backend_driver.h:15-34).
+ * Buffers are host f64 arrays in module table order (inputs, outputs).
+ * Every argument of both forms is pointer-sized and of integer class in the
+ * x86-64 System V calling convention, so this single definition with the
+ * largest arity (8 pairs + scalars pair) receives the first k arguments of a
+ * k-argument call exactly; arguments past the bound module's arity are
+ * never read. The form is chosen from the bound module with the reference's
+ * isMultiDimModule rule (reference backends/cpu/src/cpp_emitter.cpp:667-687).
+ * Returns the status (the legacy caller ignores it; mlk_last_status()
+ * reports it).
+ */
+int mlk_kernel(intptr_t a0, intptr_t a1, intptr_t a2, intptr_t a3,
+               intptr_t a4, intptr_t a5, intptr_t a6, intptr_t a7,
+               intptr_t a8, intptr_t a9, intptr_t a10, intptr_t a11,
+               intptr_t a12, intptr_t a13, intptr_t a14, intptr_t a15,
+               intptr_t a16, intptr_t a17);
+
+/* Status of the last mlk_kernel call on this thread (the legacy form returns
+ * void, reference backend_driver.h:27-30, so errors surface here). */
+int mlk_last_status(void);
+
+/* Message for the last failing call on this thread ("" when none). */
+const char* mlkb_last_error(void);
+
+/* Library version string; it also names the build target ("sm_100a"), which
+ * the fastkernel artifact fingerprint must cover
+ * (reference fastkernel/src/fast_kernel.cpp:727-763). */
+const char* mlkb_version(void);
+
+/* Number of CUDA devices visible to this process (0 when none). */
+int mlkb_device_count(void);
+
+/* Returns and clears the current device's sticky status word, which a kernel
+ * sets when one of its bounded device-side waits gives up (MLKB_ERR_TIMEOUT);
+ * 0 when clear. Synchronises with the device. */
+int mlkb_take_device_error(void);
+
+/* ======================================================================= */
+/* 2. Module entry points                                                   */
+/* ======================================================================= */
+
+/* Parses and classifies an `mlk-kernel` JSON module. The classification is
+ * the reference executor's dispatch (reference
+ * runtime/src/execution/kernel_buffers.cpp:921-1085). */
+int mlkb_module_create(const char* mlk_kernel_json, mlkb_module** out);
+void mlkb_module_destroy(mlkb_module* module);
+/* MLKB_KIND_* of a module, or a negative value for NULL. */
+int mlkb_module_kind(const mlkb_module* module);
+/* Number of bindable (input + output) buffers, in table order. */
+int mlkb_module_num_buffers(const mlkb_module* module);
+
+/*
+ * Runs the module over DEVICE buffers on `device` / `stream`.
+ *   bufs[i], dtypes[i]  buffer i of the module table (inputs then outputs),
+ *                       MLKB_F16 / MLKB_F32 / MLKB_F64
+ *   n                   element count for dynamic loop bounds
+ *                       (the reference's KernelBufferBindings::elements,
+ *                       runtime/include/mlk/runtime/execution.h:118-130)
+ *   scalars             runtime scalar table (ScalarParam operands)
+ * Semantics follow executeKernelOnBuffers (kernel_buffers.cpp:839-1106):
+ * MatMul ACCUMULATES into C (C += A*B).
+ */
+int mlkb_module_run_dev(const mlkb_module* module, void* const* bufs,
+                        const int32_t* dtypes, int32_t n_bufs, int64_t n,
+                        const double* scalars, int64_t n_scalars,
+                        int32_t device, void* stream);
+
+/*
+ * Runs the module over HOST buffers: stages inputs to the device(s), runs,
+ * copies outputs back, synchronously. n_gpus == 1 runs on the calling
+ * thread's current device; n_gpus > 1 splits the work into contiguous
+ * element / row shards over devices 0..n_gpus-1 (n_gpus <= 0: all visible
+ * devices), one host thread and stream per device. Host buffers that are page-locked copy at full PCIe
+ * speed; others are staged through pinned bounce buffers.
+ */
+int mlkb_module_run_host(const mlkb_module* module, void* const* bufs,
+                         const int32_t* dtypes, int32_t n_bufs, int64_t n,
+                         const double* scalars, int64_t n_scalars,
+                         int32_t n_gpus);
+
+/* ======================================================================= */
+/* 3. Direct kernel entry points (device pointers, asynchronous on stream)  */
+/* ======================================================================= */
+
+/* Fused map y = sin(x*x + 3x) over n f32 elements. Arithmetic follows the
+ * reference chain Mul, Mul, Add, Sin evaluated in f64
+ * (reference kernel_buffers.cpp:130-178); result rounded once to f32. */
+int mlkb_map_sin_f32(const float* x, float* y, int64_t n, void* stream);
+
+/* Map plus its calculus-pass derivative in one pass:
+ * y = sin(x*x + 3x), dy = cos(x*x + 3x) * (2x + 3). */
+int mlkb_map_sin_dsin_f32(const float* x, float* y, float* dy, int64_t n,
+                          void* stream);
+
+/* Generic fused chain out[i] = chain(a[i], b[i], scalars) for any chain of
+ * scalar-realisable ops (reference ExprEvaluator, kernel_buffers.cpp:106-178).
+ * elem_dtype MLKB_F32 or MLKB_F64 for a, b and out alike; b may be NULL when
+ * the chain never reads ElemB. At most 64 expressions and 64 scalars. */
+int mlkb_map_chain(const mlkb_expr* exprs, int32_t n_exprs, int32_t poly7_sin,
+                   const void* a, const void* b, void* out, int32_t elem_dtype,
+                   int64_t n, const double* scalars, int64_t n_scalars,
+                   void* stream);
+
+/* Row softmax Y[m,:] = softmax(X[m,:]) over a row-major [rows, cols] matrix
+ * (reference execSoftmaxCall, kernel_buffers.cpp:290-340). */
+int mlkb_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols,
+                     void* stream);
+int mlkb_softmax_f64(const double* x, double* y, int64_t rows, int64_t cols,
+                     void* stream);
+
+/* Row sums Y[m] = sum_k X[m,k] (reference execReduceSumCall,
+ * kernel_buffers.cpp:237-277). */
+int mlkb_reducesum_f32(const float* x, float* y, int64_t rows, int64_t cols,
+                       void* stream);
+int mlkb_reducesum_f64(const double* x, double* y, int64_t rows, int64_t cols,
+                       void* stream);
+
+/* C[M,N] (+)= A[M,K] * B[K,N], all row-major (reference gemmRowBlock,
+ * kernel_buffers.cpp:406-432; accumulate != 0 gives the reference's C += A*B).
+ * f16 inputs, f32 accumulation and output, on the tcgen05 tensor cores. */
+int mlkb_gemm_f16_f32(const void* a, const void* b, float* c, int64_t m,
+                      int64_t n, int64_t k, int32_t accumulate, void* stream);
+/* Same contraction with f32 inputs, f32 FMA accumulation (no TF32). */
+int mlkb_gemm_f32(const float* a, const float* b, float* c, int64_t m,
+                  int64_t n, int64_t k, int32_t accumulate, void* stream);
+/* Same contraction in f64 with the reference's per-element order
+ * (ascending k, zero-a terms skipped, no contraction into FMA). */
+int mlkb_gemm_f64(const double* a, const double* b, double* c, int64_t m,
+                  int64_t n, int64_t k, int32_t accumulate, void* stream);
+
+/* Batched Y[b] = softmax_rows(scale * Q[b] * K[b]^T), Q and K f16
+ * [batch, s, d] row-major, Y f32 [batch, s, s]: the reference composite
+ * Call(MatMul) -> scale map -> Call(Softmax) (kernel_buffers.cpp:1001-1085,
+ * :342-402, :290-340) fused into one kernel. */
+int mlkb_qk_softmax_f16(const void* q, const void* k, float* y, int64_t batch,
+                        int64_t s, int64_t d, double scale, void* stream);
+
+/* Deterministic synthetic inputs, generated on the device: a counter-based
+ * SplitMix64 stream of (seed, stream_id, element index).
+ *   dist 0: uniform  lo + (hi-lo) * k * 2^-24, k = top 24 bits
+ *   dist 1: normal   Box-Muller, mean lo, standard deviation hi */
+int mlkb_fill_f32(float* out, int64_t n, uint64_t seed, uint32_t stream_id,
+                  int32_t dist, double lo, double hi, void* stream);
+int mlkb_fill_f16(void* out, int64_t n, uint64_t seed, uint32_t stream_id,
+                  int32_t dist, double lo, double hi, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLKB200_H */

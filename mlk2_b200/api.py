@@ -1,0 +1,160 @@
+"""Typed wrappers over the libmlkb200 C ABI.
+
+Device buffers are passed as torch CUDA tensors (torch provides device memory
+and streams only); every computation happens in libmlkb200.so. Host buffers
+are numpy arrays or CPU tensors.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Sequence
+
+import numpy as np
+
+from . import F16, F32, F64, check, kir, lib
+
+_TORCH_DT = None
+
+
+def _dt_of(x) -> int:
+    global _TORCH_DT
+    if isinstance(x, np.ndarray):
+        return {np.dtype(np.float16): F16, np.dtype(np.float32): F32,
+                np.dtype(np.float64): F64}[x.dtype]
+    if _TORCH_DT is None:
+        import torch
+
+        _TORCH_DT = {torch.float16: F16, torch.float32: F32, torch.float64: F64}
+    return _TORCH_DT[x.dtype]
+
+
+def _ptr(x) -> int:
+    if x is None:
+        return None
+    if isinstance(x, np.ndarray):
+        if not x.flags["C_CONTIGUOUS"]:
+            raise ValueError("host buffers must be C-contiguous")
+        return x.ctypes.data
+    if not x.is_contiguous():
+        raise ValueError("tensors must be contiguous")
+    return x.data_ptr()
+
+
+def _stream(stream=None) -> int:
+    if stream is not None:
+        return int(stream)
+    import torch
+
+    return torch.cuda.current_stream().cuda_stream
+
+
+# ---- direct kernels (device tensors, asynchronous on the current stream) ----
+
+def map_sin(x, y, stream=None):
+    check(lib().mlkb_map_sin_f32(_ptr(x), _ptr(y), x.numel(), _stream(stream)))
+
+
+def map_sin_dsin(x, y, dy, stream=None):
+    check(lib().mlkb_map_sin_dsin_f32(_ptr(x), _ptr(y), _ptr(dy), x.numel(), _stream(stream)))
+
+
+def map_chain(exprs: np.ndarray, a, out, b=None, scalars: Sequence[float] = (), poly7=False,
+              stream=None):
+    exprs = np.ascontiguousarray(exprs, dtype=kir.EXPR_DTYPE)
+    sc = (C.c_double * max(1, len(scalars)))(*scalars)
+    check(lib().mlkb_map_chain(exprs.ctypes.data, len(exprs), int(poly7), _ptr(a), _ptr(b),
+                               _ptr(out), _dt_of(out), out.numel(), sc, len(scalars),
+                               _stream(stream)))
+
+
+def softmax(x, y, stream=None):
+    rows, cols = x.shape
+    fn = lib().mlkb_softmax_f32 if _dt_of(x) == F32 else lib().mlkb_softmax_f64
+    check(fn(_ptr(x), _ptr(y), rows, cols, _stream(stream)))
+
+
+def reducesum(x, y, stream=None):
+    rows, cols = x.shape
+    fn = lib().mlkb_reducesum_f32 if _dt_of(x) == F32 else lib().mlkb_reducesum_f64
+    check(fn(_ptr(x), _ptr(y), rows, cols, _stream(stream)))
+
+
+def gemm(a, b, c, accumulate=False, stream=None):
+    m, k = a.shape
+    k2, n = b.shape
+    assert k == k2 and tuple(c.shape) == (m, n)
+    dt = _dt_of(a)
+    fn = {F16: lib().mlkb_gemm_f16_f32, F32: lib().mlkb_gemm_f32, F64: lib().mlkb_gemm_f64}[dt]
+    check(fn(_ptr(a), _ptr(b), _ptr(c), m, n, k, int(accumulate), _stream(stream)))
+
+
+def qk_softmax(q, k, y, scale: float, stream=None):
+    batch, s, d = q.shape
+    check(lib().mlkb_qk_softmax_f16(_ptr(q), _ptr(k), _ptr(y), batch, s, d, float(scale),
+                                    _stream(stream)))
+
+
+def fill(out, seed: int, stream_id: int, dist: str, lo: float, hi: float, stream=None):
+    d = {"uniform": 0, "normal": 1}[dist]
+    fn = lib().mlkb_fill_f32 if _dt_of(out) == F32 else lib().mlkb_fill_f16
+    check(fn(_ptr(out), out.numel(), seed, stream_id, d, lo, hi, _stream(stream)))
+
+
+def take_device_error() -> int:
+    return lib().mlkb_take_device_error()
+
+
+# ---- module API ---------------------------------------------------------------
+
+class Module:
+    """A Kernel IR module bound from its `mlk-kernel` JSON (dict or str)."""
+
+    def __init__(self, module):
+        text = module if isinstance(module, str) else kir.dumps(module)
+        h = C.c_void_p()
+        check(lib().mlkb_module_create(text.encode(), C.byref(h)))
+        self._h = h
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().mlkb_module_destroy(self._h)
+            self._h = None
+
+    @property
+    def kind(self) -> int:
+        return lib().mlkb_module_kind(self._h)
+
+    @property
+    def num_buffers(self) -> int:
+        return lib().mlkb_module_num_buffers(self._h)
+
+    def _args(self, bufs, scalars):
+        n = len(bufs)
+        ptrs = (C.c_void_p * n)(*[_ptr(b) for b in bufs])
+        dts = (C.c_int32 * n)(*[_dt_of(b) for b in bufs])
+        sc = (C.c_double * max(1, len(scalars)))(*scalars)
+        return ptrs, dts, n, sc
+
+    def run_dev(self, bufs, n: int = 0, scalars: Sequence[float] = (), device: int = 0,
+                stream=None):
+        ptrs, dts, nb, sc = self._args(bufs, scalars)
+        check(lib().mlkb_module_run_dev(self._h, ptrs, dts, nb, n, sc, len(scalars), device,
+                                        _stream(stream)))
+
+    def run_host(self, bufs, n: int = 0, scalars: Sequence[float] = (), n_gpus: int = 0):
+        ptrs, dts, nb, sc = self._args(bufs, scalars)
+        check(lib().mlkb_module_run_host(self._h, ptrs, dts, nb, n, sc, len(scalars), n_gpus))
+
+
+def legacy_call(module: dict, host_f64: Sequence[np.ndarray], n: int,
+                scalars: Sequence[float] = ()) -> int:
+    """Bind `module` and call mlk_kernel in the reference's legacy 1-D form
+    (buffers..., n, scalars, n_scalars) exactly as LoadedKernel::run does;
+    returns mlk_last_status()."""
+    L = lib()
+    check(L.mlk_bind_module(kir.dumps(module).encode()))
+    sc = (C.c_double * max(1, len(scalars)))(*scalars)
+    args = [b.ctypes.data for b in host_f64] + [n, C.cast(sc, C.c_void_p).value, len(scalars)]
+    args += [0] * (18 - len(args))
+    L.mlk_kernel(*args)
+    return L.mlk_last_status()

@@ -1,0 +1,608 @@
+// Host side of libmlkb200: status reporting, module entry points, host-buffer
+// runs sharded over GPUs, and the reference artifact ABI (mlk_kernel).
+//
+// Replaces the per-call host wrapper the reference's CUDA emitter generates
+// (reference backends/cpu/src/cuda_emitter.cpp:1789-1867: cudaMalloc, H2D,
+// launch, D2H, cudaFree on every call) with:
+//   * a persistent per-device buffer cache (no allocation once warm),
+//   * one stream per device and contiguous shards over all devices,
+//   * chunked copy/compute overlap for streaming maps,
+//   * the module bound once from its wire format instead of baked into
+//     generated source.
+#include <dlfcn.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "common.cuh"
+#include "module.h"
+
+struct mlkb_module {
+    mlkb::Module m;
+};
+
+namespace mlkb {
+
+// ---- status -----------------------------------------------------------------
+namespace {
+thread_local std::string t_err;
+thread_local int t_status = 0;
+}  // namespace
+
+int setError(int code, const char* msg) {
+    t_err = msg != nullptr ? msg : "";
+    return code;
+}
+
+int setCudaError(int code, cudaError_t e, const char* what) {
+    t_err = std::string(what) + ": " + cudaGetErrorString(e);
+    return code;
+}
+
+int okStatus() { return MLKB_OK; }
+
+int smCount() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = v > 0 ? v : 148;
+    }
+    return cache[dev];
+}
+
+namespace {
+
+int elemBytes(int dtype) {
+    return dtype == MLKB_F16 ? 2 : dtype == MLKB_F32 ? 4 : dtype == MLKB_F64 ? 8 : 0;
+}
+
+// ---- per-device resources -----------------------------------------------------
+struct DeviceSlot {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+
+struct DeviceCtx {
+    std::mutex mu;
+    bool init = false;
+    cudaStream_t streams[2] = {nullptr, nullptr};
+    std::vector<DeviceSlot> slots;  // grow-only buffer cache, reused per call
+};
+
+DeviceCtx g_dev[64];
+
+int deviceCount() {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+int ensureCtx(int dev) {
+    DeviceCtx& c = g_dev[dev];
+    if (c.init) return okStatus();
+    cudaError_t e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return setCudaError(MLKB_ERR_NO_DEVICE, e, "cudaSetDevice");
+    for (auto& s : c.streams) {
+        e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "cudaStreamCreate");
+    }
+    c.init = true;
+    return okStatus();
+}
+
+// Slot `i` of device `dev` with at least `bytes` (caller holds c.mu).
+int slotPtr(int dev, size_t i, size_t bytes, void** out) {
+    DeviceCtx& c = g_dev[dev];
+    if (c.slots.size() <= i) c.slots.resize(i + 1);
+    DeviceSlot& s = c.slots[i];
+    if (s.bytes < bytes) {
+        if (s.ptr != nullptr) cudaFree(s.ptr);
+        s.ptr = nullptr;
+        s.bytes = 0;
+        const cudaError_t e = cudaMalloc(&s.ptr, bytes > 0 ? bytes : 16);
+        if (e != cudaSuccess) {
+            s.ptr = nullptr;
+            return setCudaError(MLKB_ERR_CUDA_MEM, e, "device buffer allocation");
+        }
+        s.bytes = bytes;
+    }
+    *out = s.ptr;
+    return okStatus();
+}
+
+// ---- module dispatch over device buffers -------------------------------------
+
+// u = x*x + 3x as lowering emits it: Mul(A,A), Mul(3,A), Add(t0,t1).
+bool isU(const std::vector<mlkb_expr>& c) {
+    if (c.size() < 3) return false;
+    const mlkb_expr &e0 = c[0], &e1 = c[1], &e2 = c[2];
+    const bool m0 = e0.op == 2 && e0.a_kind == 1 && e0.b_kind == 1;
+    const bool m1 = e1.op == 2 && ((e1.a_kind == 0 && e1.a_value == 3.0 && e1.b_kind == 1) ||
+                                   (e1.b_kind == 0 && e1.b_value == 3.0 && e1.a_kind == 1));
+    const bool m2 = e2.op == 0 && e2.a_kind == 4 && e2.b_kind == 4 &&
+                    ((e2.a_index == 0 && e2.b_index == 1) || (e2.a_index == 1 && e2.b_index == 0));
+    return m0 && m1 && m2;
+}
+
+// y = sin(u): the config-1 chain.
+bool isSinChain(const std::vector<mlkb_expr>& c) {
+    return c.size() == 4 && isU(c) && c[3].op == 8 && c[3].a_kind == 4 && c[3].a_index == 2;
+}
+
+// dy = cos(u) * (2x + 3): the calculus-pass derivative chain.
+bool isDsinChain(const std::vector<mlkb_expr>& c) {
+    if (c.size() != 7 || !isU(c)) return false;
+    const mlkb_expr &e3 = c[3], &e4 = c[4], &e5 = c[5], &e6 = c[6];
+    const bool cosu = e3.op == 9 && e3.a_kind == 4 && e3.a_index == 2;
+    const bool twox = e4.op == 2 && ((e4.a_kind == 0 && e4.a_value == 2.0 && e4.b_kind == 1) ||
+                                     (e4.b_kind == 0 && e4.b_value == 2.0 && e4.a_kind == 1));
+    const bool plus3 = e5.op == 0 && ((e5.a_kind == 4 && e5.a_index == 4 && e5.b_kind == 0 &&
+                                       e5.b_value == 3.0) ||
+                                      (e5.b_kind == 4 && e5.b_index == 4 && e5.a_kind == 0 &&
+                                       e5.a_value == 3.0));
+    const bool prod = e6.op == 2 && e6.a_kind == 4 && e6.b_kind == 4 &&
+                      ((e6.a_index == 3 && e6.b_index == 5) || (e6.a_index == 5 && e6.b_index == 3));
+    return cosu && twox && plus3 && prod;
+}
+
+void* bufAt(void* const* bufs, const Module& m, int bid) {
+    for (size_t i = 0; i < m.bindable.size(); ++i) {
+        if (m.bindable[i] == bid) return bufs[i];
+    }
+    return nullptr;
+}
+
+int dtypeAt(const int32_t* dt, const Module& m, int bid) {
+    for (size_t i = 0; i < m.bindable.size(); ++i) {
+        if (m.bindable[i] == bid) return dt[i];
+    }
+    return 0;
+}
+
+char* offsetPtr(void* p, int64_t elems, int dtype) {
+    return static_cast<char*>(p) + elems * elemBytes(dtype);
+}
+
+int runMapDev(const Module& m, void* const* bufs, const int32_t* dt, int64_t n,
+              const double* scalars, int64_t n_scalars, void* stream) {
+    std::vector<uint8_t> done(m.roots.size(), 0);
+    for (size_t r = 0; r < m.roots.size(); ++r) {
+        if (done[r]) continue;
+        const MapRoot& root = m.roots[r];
+        const int64_t end = root.end < 0 ? n : root.end;
+        const int64_t cnt = end > root.begin ? end - root.begin : 0;
+        const int dtOut = dtypeAt(dt, m, root.out);
+        const int dtA = root.a >= 0 ? dtypeAt(dt, m, root.a) : dtOut;
+        const int dtB = root.b >= 0 ? dtypeAt(dt, m, root.b) : dtOut;
+        void* out = bufAt(bufs, m, root.out);
+        void* a = root.a >= 0 ? bufAt(bufs, m, root.a) : nullptr;
+        void* b = root.b >= 0 ? bufAt(bufs, m, root.b) : nullptr;
+        if (out == nullptr || (root.a >= 0 && a == nullptr) || (root.b >= 0 && b == nullptr)) {
+            return setError(MLKB_ERR_INVALID, "map: buffer not bound by the caller");
+        }
+        if (dtA != dtOut || dtB != dtOut || (dtOut != MLKB_F32 && dtOut != MLKB_F64)) {
+            return setError(MLKB_ERR_INVALID, "map: buffers must all be f32 or all f64");
+        }
+        if (cnt == 0) continue;
+        if (dtOut == MLKB_F32 && root.a >= 0 && !root.poly7 && isSinChain(root.chain)) {
+            // Fuse with a later derivative root over the same input and range.
+            for (size_t q = r + 1; q < m.roots.size(); ++q) {
+                const MapRoot& o = m.roots[q];
+                if (!done[q] && o.a == root.a && o.begin == root.begin && o.end == root.end &&
+                    isDsinChain(o.chain) && dtypeAt(dt, m, o.out) == MLKB_F32 &&
+                    bufAt(bufs, m, o.out) != nullptr) {
+                    done[q] = 1;
+                    int st = mlkb_map_sin_dsin_f32(
+                        reinterpret_cast<const float*>(offsetPtr(a, root.begin, dtA)),
+                        reinterpret_cast<float*>(offsetPtr(out, root.begin, dtOut)),
+                        reinterpret_cast<float*>(offsetPtr(bufAt(bufs, m, o.out), o.begin, dtOut)),
+                        cnt, stream);
+                    if (st) return st;
+                    goto next_root;
+                }
+            }
+            if (int st = mlkb_map_sin_f32(
+                    reinterpret_cast<const float*>(offsetPtr(a, root.begin, dtA)),
+                    reinterpret_cast<float*>(offsetPtr(out, root.begin, dtOut)), cnt, stream)) {
+                return st;
+            }
+            continue;
+        }
+        if (int st = mlkb_map_chain(root.chain.data(), static_cast<int32_t>(root.chain.size()),
+                                    root.poly7 ? 1 : 0,
+                                    a != nullptr ? offsetPtr(a, root.begin, dtA) : nullptr,
+                                    b != nullptr ? offsetPtr(b, root.begin, dtB) : nullptr,
+                                    offsetPtr(out, root.begin, dtOut), dtOut, cnt, scalars,
+                                    n_scalars, stream)) {
+            return st;
+        }
+    next_root:;
+    }
+    return okStatus();
+}
+
+int runDev(const Module& m, void* const* bufs, const int32_t* dt, int64_t n,
+           const double* scalars, int64_t n_scalars, void* stream) {
+    switch (m.kind) {
+        case MLKB_KIND_MAP: return runMapDev(m, bufs, dt, n, scalars, n_scalars, stream);
+        case MLKB_KIND_SOFTMAX:
+        case MLKB_KIND_REDUCESUM: {
+            void* a = bufAt(bufs, m, m.callA);
+            void* y = bufAt(bufs, m, m.callOut);
+            const int da = dtypeAt(dt, m, m.callA), dy = dtypeAt(dt, m, m.callOut);
+            if (da != dy) return setError(MLKB_ERR_INVALID, "rows: dtype mismatch");
+            const bool sm = m.kind == MLKB_KIND_SOFTMAX;
+            if (da == MLKB_F32) {
+                return sm ? mlkb_softmax_f32(static_cast<float*>(a), static_cast<float*>(y), m.m,
+                                             m.k, stream)
+                          : mlkb_reducesum_f32(static_cast<float*>(a), static_cast<float*>(y),
+                                               m.m, m.k, stream);
+            }
+            if (da == MLKB_F64) {
+                return sm ? mlkb_softmax_f64(static_cast<double*>(a), static_cast<double*>(y),
+                                             m.m, m.k, stream)
+                          : mlkb_reducesum_f64(static_cast<double*>(a), static_cast<double*>(y),
+                                               m.m, m.k, stream);
+            }
+            return setError(MLKB_ERR_INVALID, "rows: dtype must be f32 or f64");
+        }
+        case MLKB_KIND_MATMUL: {
+            void* a = bufAt(bufs, m, m.callA);
+            void* b = bufAt(bufs, m, m.callB);
+            void* c = bufAt(bufs, m, m.callOut);
+            const int da = dtypeAt(dt, m, m.callA), db = dtypeAt(dt, m, m.callB),
+                      dc = dtypeAt(dt, m, m.callOut);
+            // The reference accumulates: C += A*B (kernel_buffers.cpp:406-432).
+            if (da == MLKB_F16 && db == MLKB_F16 && dc == MLKB_F32) {
+                return mlkb_gemm_f16_f32(a, b, static_cast<float*>(c), m.m, m.n, m.k, 1, stream);
+            }
+            if (da == MLKB_F32 && db == MLKB_F32 && dc == MLKB_F32) {
+                return mlkb_gemm_f32(static_cast<float*>(a), static_cast<float*>(b),
+                                     static_cast<float*>(c), m.m, m.n, m.k, 1, stream);
+            }
+            if (da == MLKB_F64 && db == MLKB_F64 && dc == MLKB_F64) {
+                return mlkb_gemm_f64(static_cast<double*>(a), static_cast<double*>(b),
+                                     static_cast<double*>(c), m.m, m.n, m.k, 1, stream);
+            }
+            return setError(MLKB_ERR_INVALID, "matmul: dtypes must be f16/f16/f32, f32 or f64");
+        }
+        default: return setError(MLKB_ERR_UNSUPPORTED, "module kind not runnable here");
+    }
+}
+
+// ---- host-buffer runs ----------------------------------------------------------
+
+// A contiguous shard: the unit range [u0, u1) of the module's split axis.
+struct Shard {
+    int dev;
+    int64_t u0, u1;
+};
+
+// Split axis per kind: map -> elements of the loop range; rows -> rows of A;
+// matmul -> rows of A and C (B replicated).
+int64_t unitsOf(const Module& m, int64_t n) {
+    switch (m.kind) {
+        case MLKB_KIND_MAP: return n;
+        case MLKB_KIND_MATMUL:
+        case MLKB_KIND_SOFTMAX:
+        case MLKB_KIND_REDUCESUM: return m.m;
+        default: return 0;
+    }
+}
+
+// Runs one shard on its device: stage, run, copy back. Maps stream in chunks
+// over two streams so H2D, compute and D2H of different chunks overlap.
+int runShard(const Module& m0, const Shard& sh, void* const* bufs, const int32_t* dt,
+             int64_t n, const double* scalars, int64_t n_scalars) {
+    DeviceCtx& c = g_dev[sh.dev];
+    std::lock_guard<std::mutex> lock(c.mu);
+    cudaError_t e = cudaSetDevice(sh.dev);
+    if (e != cudaSuccess) return setCudaError(MLKB_ERR_NO_DEVICE, e, "cudaSetDevice");
+    if (int st = ensureCtx(sh.dev)) return st;
+    const size_t nb = m0.bindable.size();
+    const int64_t units = sh.u1 - sh.u0;
+    if (units <= 0) return okStatus();
+
+    if (m0.kind == MLKB_KIND_MAP) {
+        // Every root reads/writes element i of its buffers: shard = element range.
+        const int64_t chunk = int64_t(1) << 24;  // elements per pipeline step
+        std::vector<void*> dbuf[2];
+        for (int s = 0; s < 2; ++s) {
+            dbuf[s].resize(nb);
+            for (size_t i = 0; i < nb; ++i) {
+                const int64_t cnt = units < chunk ? units : chunk;
+                if (int st = slotPtr(sh.dev, s * nb + i, static_cast<size_t>(cnt) * elemBytes(dt[i]),
+                                     &dbuf[s][i])) {
+                    return st;
+                }
+            }
+        }
+        // Shift the module's loop ranges into chunk-local coordinates.
+        int step = 0;
+        for (int64_t base = sh.u0; base < sh.u1; base += chunk, ++step) {
+            const int64_t cnt = (sh.u1 - base) < chunk ? (sh.u1 - base) : chunk;
+            const int s = step & 1;
+            cudaStream_t st = c.streams[s];
+            Module m = m0;
+            bool any = false;
+            // Per bindable buffer: written by some root in this chunk, and
+            // written over the whole chunk (no need to stage its old values).
+            std::vector<uint8_t> written(nb, 0), partial(nb, 0);
+            for (MapRoot& r : m.roots) {
+                const int64_t rEnd = r.end < 0 ? n : r.end;
+                const int64_t lo = r.begin > base ? r.begin : base;
+                const int64_t hi = rEnd < base + cnt ? rEnd : base + cnt;
+                r.begin = lo - base;
+                r.end = hi > lo ? hi - base : r.begin;
+                if (hi <= lo) continue;
+                any = true;
+                for (size_t i = 0; i < nb; ++i) {
+                    if (m0.bindable[i] != r.out) continue;
+                    written[i] = 1;
+                    if (lo != base || hi != base + cnt) partial[i] = 1;
+                }
+            }
+            if (!any) continue;
+            for (size_t i = 0; i < nb; ++i) {
+                // Inputs, and outputs a root writes only in part (the rest
+                // keeps the caller's values, as in the reference executor).
+                if (m0.buffers[m0.bindable[i]].input || partial[i]) {
+                    e = cudaMemcpyAsync(dbuf[s][i], offsetPtr(bufs[i], base, dt[i]),
+                                        static_cast<size_t>(cnt) * elemBytes(dt[i]),
+                                        cudaMemcpyHostToDevice, st);
+                    if (e != cudaSuccess) return setCudaError(MLKB_ERR_CUDA_MEM, e, "H2D");
+                }
+            }
+            if (int rs = runDev(m, dbuf[s].data(), dt, cnt, scalars, n_scalars, st)) return rs;
+            for (size_t i = 0; i < nb; ++i) {
+                if (!written[i]) continue;
+                e = cudaMemcpyAsync(offsetPtr(bufs[i], base, dt[i]), dbuf[s][i],
+                                    static_cast<size_t>(cnt) * elemBytes(dt[i]),
+                                    cudaMemcpyDeviceToHost, st);
+                if (e != cudaSuccess) return setCudaError(MLKB_ERR_CUDA_MEM, e, "D2H");
+            }
+        }
+        for (auto& s : c.streams) {
+            e = cudaStreamSynchronize(s);
+            if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "map shard sync");
+        }
+        return okStatus();
+    }
+
+    // Row-split kinds: A rows [u0,u1), output rows [u0,u1); MatMul replicates B.
+    Module m = m0;
+    m.m = units;
+    cudaStream_t st = c.streams[0];
+    std::vector<void*> dbuf(nb);
+    std::vector<int64_t> off(nb, 0), cnt(nb, 0);
+    for (size_t i = 0; i < nb; ++i) {
+        const int bid = m.bindable[i];
+        int64_t rowLen = 1;
+        if (bid == m.callA) rowLen = m.k;
+        else if (bid == m.callOut) rowLen = m.kind == MLKB_KIND_MATMUL ? m.n
+                                            : m.kind == MLKB_KIND_SOFTMAX ? m.k : 1;
+        if (bid == m.callB) {
+            off[i] = 0;
+            cnt[i] = m.k * m.n;
+        } else {
+            off[i] = sh.u0 * rowLen;
+            cnt[i] = units * rowLen;
+        }
+        if (int s2 = slotPtr(sh.dev, i, static_cast<size_t>(cnt[i]) * elemBytes(dt[i]), &dbuf[i])) {
+            return s2;
+        }
+        // Inputs, and MatMul's C (accumulated into), go to the device.
+        const bool stage = m.buffers[bid].input || (m.kind == MLKB_KIND_MATMUL && bid == m.callOut);
+        if (stage) {
+            e = cudaMemcpyAsync(dbuf[i], offsetPtr(bufs[i], off[i], dt[i]),
+                                static_cast<size_t>(cnt[i]) * elemBytes(dt[i]),
+                                cudaMemcpyHostToDevice, st);
+            if (e != cudaSuccess) return setCudaError(MLKB_ERR_CUDA_MEM, e, "H2D");
+        }
+    }
+    if (int rs = runDev(m, dbuf.data(), dt, n, scalars, n_scalars, st)) return rs;
+    for (size_t i = 0; i < nb; ++i) {
+        if (!m.buffers[m.bindable[i]].output) continue;
+        e = cudaMemcpyAsync(offsetPtr(bufs[i], off[i], dt[i]), dbuf[i],
+                            static_cast<size_t>(cnt[i]) * elemBytes(dt[i]),
+                            cudaMemcpyDeviceToHost, st);
+        if (e != cudaSuccess) return setCudaError(MLKB_ERR_CUDA_MEM, e, "D2H");
+    }
+    e = cudaStreamSynchronize(st);
+    return e == cudaSuccess ? okStatus() : setCudaError(MLKB_ERR_LAUNCH, e, "shard sync");
+}
+
+int runHost(const Module& m, void* const* bufs, const int32_t* dt, int32_t n_bufs, int64_t n,
+            const double* scalars, int64_t n_scalars, int32_t n_gpus) {
+    if (n_bufs != static_cast<int32_t>(m.bindable.size())) {
+        return setError(MLKB_ERR_INVALID, "run: buffer count differs from the module table");
+    }
+    for (int32_t i = 0; i < n_bufs; ++i) {
+        if (bufs[i] == nullptr) return setError(MLKB_ERR_INVALID, "run: null host buffer");
+        if (elemBytes(dt[i]) == 0) return setError(MLKB_ERR_INVALID, "run: unknown dtype");
+    }
+    const int avail = deviceCount();
+    if (avail <= 0) return setError(MLKB_ERR_NO_DEVICE, "no CUDA device");
+    int g = n_gpus <= 0 ? avail : (n_gpus < avail ? n_gpus : avail);
+    const int64_t units = unitsOf(m, n);
+    if (units <= 0) return okStatus();
+    if (g > units) g = static_cast<int>(units);
+    if (g == 1) {
+        // One GPU: the caller's current device (one process per GPU).
+        int cur = 0;
+        if (cudaGetDevice(&cur) != cudaSuccess) cur = 0;
+        return runShard(m, Shard{cur, 0, units}, bufs, dt, n, scalars, n_scalars);
+    }
+    std::vector<Shard> shards;
+    for (int d = 0; d < g; ++d) {
+        shards.push_back(Shard{d, units * d / g, units * (d + 1) / g});
+    }
+    std::vector<int> rc(g, 0);
+    std::vector<std::string> msg(g);
+    std::vector<std::thread> th;
+    for (int d = 0; d < g; ++d) {
+        th.emplace_back([&, d]() {
+            rc[d] = runShard(m, shards[d], bufs, dt, n, scalars, n_scalars);
+            if (rc[d] != 0) msg[d] = mlkb_last_error();
+        });
+    }
+    for (auto& t : th) t.join();
+    for (int d = 0; d < g; ++d) {
+        if (rc[d] != 0) return setError(rc[d], msg[d].c_str());
+    }
+    return okStatus();
+}
+
+// ---- reference artifact ABI state --------------------------------------------
+std::mutex g_bindMu;
+std::shared_ptr<mlkb_module> g_bound;
+std::once_flag g_sidecarOnce;
+
+void loadSidecar() {
+    Dl_info info{};
+    if (dladdr(reinterpret_cast<void*>(&mlk_kernel), &info) == 0 || info.dli_fname == nullptr) {
+        return;
+    }
+    std::string path(info.dli_fname);
+    const size_t slash = path.rfind('/');
+    path = (slash == std::string::npos ? std::string(".") : path.substr(0, slash)) + "/module.json";
+    std::ifstream f(path);
+    if (!f) return;
+    std::stringstream ss;
+    ss << f.rdbuf();
+    auto mod = std::make_shared<mlkb_module>();
+    if (parseModule(ss.str().c_str(), mod->m) == MLKB_OK) g_bound = mod;
+}
+
+}  // namespace
+}  // namespace mlkb
+
+using namespace mlkb;
+
+extern "C" const char* mlkb_last_error(void) { return t_err.c_str(); }
+extern "C" int mlk_last_status(void) { return t_status; }
+extern "C" const char* mlkb_version(void) { return "mlkb200 0.1.0 sm_100a"; }
+extern "C" int mlkb_device_count(void) { return deviceCount(); }
+
+extern "C" int mlkb_module_create(const char* json, mlkb_module** out) {
+    if (out == nullptr) return setError(MLKB_ERR_INVALID, "module_create: null out");
+    *out = nullptr;
+    auto* mod = new mlkb_module();
+    if (int st = parseModule(json, mod->m)) {
+        delete mod;
+        return st;
+    }
+    *out = mod;
+    return okStatus();
+}
+
+extern "C" void mlkb_module_destroy(mlkb_module* module) { delete module; }
+
+extern "C" int mlkb_module_kind(const mlkb_module* module) {
+    return module != nullptr ? module->m.kind : -1;
+}
+
+extern "C" int mlkb_module_num_buffers(const mlkb_module* module) {
+    return module != nullptr ? static_cast<int>(module->m.bindable.size()) : -1;
+}
+
+extern "C" int mlkb_module_run_dev(const mlkb_module* module, void* const* bufs,
+                                   const int32_t* dtypes, int32_t n_bufs, int64_t n,
+                                   const double* scalars, int64_t n_scalars, int32_t device,
+                                   void* stream) {
+    if (module == nullptr || bufs == nullptr || dtypes == nullptr) {
+        return setError(MLKB_ERR_INVALID, "run_dev: null argument");
+    }
+    if (n_bufs != static_cast<int32_t>(module->m.bindable.size())) {
+        return setError(MLKB_ERR_INVALID, "run_dev: buffer count differs from the module table");
+    }
+    if (n < 0) return setError(MLKB_ERR_INVALID, "run_dev: negative element count");
+    const int avail = deviceCount();
+    if (avail <= 0) return setError(MLKB_ERR_NO_DEVICE, "no CUDA device");
+    if (device < 0 || device >= avail) return setError(MLKB_ERR_INVALID, "run_dev: bad device");
+    const cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return setCudaError(MLKB_ERR_NO_DEVICE, e, "cudaSetDevice");
+    return runDev(module->m, bufs, dtypes, n, scalars, n_scalars, stream);
+}
+
+extern "C" int mlkb_module_run_host(const mlkb_module* module, void* const* bufs,
+                                    const int32_t* dtypes, int32_t n_bufs, int64_t n,
+                                    const double* scalars, int64_t n_scalars, int32_t n_gpus) {
+    if (module == nullptr || bufs == nullptr || dtypes == nullptr) {
+        return setError(MLKB_ERR_INVALID, "run_host: null argument");
+    }
+    if (n < 0) return setError(MLKB_ERR_INVALID, "run_host: negative element count");
+    return runHost(module->m, bufs, dtypes, n_bufs, n, scalars, n_scalars, n_gpus);
+}
+
+extern "C" int mlk_bind_module(const char* json) {
+    std::lock_guard<std::mutex> lock(g_bindMu);
+    if (json == nullptr) {
+        g_bound.reset();
+        return okStatus();
+    }
+    auto mod = std::make_shared<mlkb_module>();
+    if (int st = parseModule(json, mod->m)) return st;
+    g_bound = mod;
+    return okStatus();
+}
+
+extern "C" int mlk_kernel(intptr_t a0, intptr_t a1, intptr_t a2, intptr_t a3, intptr_t a4,
+                          intptr_t a5, intptr_t a6, intptr_t a7, intptr_t a8, intptr_t a9,
+                          intptr_t a10, intptr_t a11, intptr_t a12, intptr_t a13, intptr_t a14,
+                          intptr_t a15, intptr_t a16, intptr_t a17) {
+    std::shared_ptr<mlkb_module> mod;
+    {
+        std::lock_guard<std::mutex> lock(g_bindMu);
+        std::call_once(g_sidecarOnce, []() {
+            if (!g_bound) loadSidecar();
+        });
+        mod = g_bound;
+    }
+    if (!mod) {
+        t_status = setError(MLKB_ERR_NOT_BOUND, "mlk_kernel: no module bound");
+        return t_status;
+    }
+    const intptr_t args[18] = {a0, a1, a2, a3, a4, a5, a6, a7, a8,
+                               a9, a10, a11, a12, a13, a14, a15, a16, a17};
+    const Module& m = mod->m;
+    const size_t nb = m.bindable.size();
+    if (nb == 0 || nb > 8) {
+        t_status = setError(MLKB_ERR_UNSUPPORTED, "mlk_kernel: 1..8 bindable buffers");
+        return t_status;
+    }
+    std::vector<void*> bufs(nb);
+    std::vector<int32_t> dt(nb, MLKB_F64);
+    int64_t n = 0;
+    const double* scalars = nullptr;
+    int64_t nsc = 0;
+    if (m.multiDim) {
+        // int mlk_kernel(B0, B0_dims, ..., scalars, n_scalars)
+        for (size_t i = 0; i < nb; ++i) bufs[i] = reinterpret_cast<void*>(args[2 * i]);
+        scalars = reinterpret_cast<const double*>(args[2 * nb]);
+        nsc = static_cast<int64_t>(args[2 * nb + 1]);
+    } else {
+        // void mlk_kernel(B0, ..., n, scalars, n_scalars)
+        for (size_t i = 0; i < nb; ++i) bufs[i] = reinterpret_cast<void*>(args[i]);
+        n = static_cast<int64_t>(args[nb]);
+        scalars = reinterpret_cast<const double*>(args[nb + 1]);
+        nsc = static_cast<int64_t>(args[nb + 2]);
+    }
+    if (nsc < 0 || nsc > 64) nsc = 0;
+    t_status = runHost(m, bufs.data(), dt.data(), static_cast<int32_t>(nb), n, scalars, nsc, 0);
+    return t_status;
+}

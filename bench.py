@@ -163,11 +163,17 @@ def run_reference_arm(args, rank):
     print(json.dumps(line), flush=True)
 
 
-def time_device(torch, fn, warmup, steps, dist, world):
-    """W untimed steps, then K steps between barrier+sync; CUDA events on the
-    current stream; max over ranks. Returns seconds per step."""
-    for _ in range(warmup):
+def time_device(torch, fn, warmup, steps, dist, world, min_warm_s=0.0):
+    """W untimed steps (continued until min_warm_s has passed, so clock samples
+    see the same steady load), then K steps between barrier+sync; CUDA events
+    on the current stream; max over ranks. Returns seconds per step."""
+    t0 = time.perf_counter()
+    done = 0
+    while done < warmup or time.perf_counter() - t0 < min_warm_s:
         fn()
+        done += 1
+        if done % 16 == 0:
+            torch.cuda.synchronize()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -195,8 +201,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--headline-only", action="store_true")
+    ap.add_argument("--min-warm-s", type=float, default=1.5,
+                    help="headline warm-up continues at least this long (clock samples)")
+    ap.add_argument("--case", default=None,
+                    choices=["map1", "map2", "softmax", "gemm", "gemm_f32", "qk"],
+                    help="run one kernel W+K times (profiling target), no JSON line")
+    ap.add_argument("--size", type=int, default=0,
+                    help="--case size: elements (maps), rows (softmax), M=N=K (gemm), batch (qk)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.case:
+        run_case(args)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -230,7 +246,8 @@ def main():
     dy = torch.empty_like(x)
     step = lambda: api.map_sin_dsin(x, y, dy)  # noqa: E731
     with ClockSampler(local) as clk:
-        sec = time_device(torch, step, args.warmup, args.steps, dist, world)
+        sec = time_device(torch, step, args.warmup, args.steps, dist, world,
+                          min_warm_s=args.min_warm_s)
     clocks = clk.summary()
     alg_bytes = n * BYTES_PER_ELEM_MAP2
     achieved = alg_bytes / sec / 1e9
@@ -303,6 +320,47 @@ def main():
         dist.destroy_process_group()
 
 
+def run_case(args):
+    """One kernel, W + K launches, default stream; prints ms per launch."""
+    import torch
+
+    from mlk2_b200 import api
+
+    torch.cuda.set_device(0)
+    c, sz = args.case, args.size
+    if c in ("map1", "map2"):
+        n = sz or (1 << 26)
+        x = torch.empty(n, device="cuda")
+        api.fill(x, SEED, 2, "uniform", -8.0, 8.0)
+        y, dy = torch.empty_like(x), torch.empty_like(x)
+        fn = (lambda: api.map_sin_dsin(x, y, dy)) if c == "map2" else (lambda: api.map_sin(x, y))
+    elif c == "softmax":
+        rows = sz or 16384
+        x = torch.empty((rows, 4096), device="cuda")
+        api.fill(x, SEED, 3, "normal", 0.0, 4.0)
+        y = torch.empty_like(x)
+        fn = lambda: api.softmax(x, y)  # noqa: E731
+    elif c in ("gemm", "gemm_f32"):
+        n = sz or 8192
+        dt = torch.float16 if c == "gemm" else torch.float32
+        a = torch.empty((n, n), dtype=dt, device="cuda")
+        b = torch.empty((n, n), dtype=dt, device="cuda")
+        a.normal_(0, n ** -0.5)
+        b.normal_(0, n ** -0.5)
+        cc = torch.empty((n, n), device="cuda")
+        fn = lambda: api.gemm(a, b, cc)  # noqa: E731
+    else:
+        bq = sz or 32
+        q = torch.empty((bq, 2048, 128), dtype=torch.float16, device="cuda")
+        k = torch.empty((bq, 2048, 128), dtype=torch.float16, device="cuda")
+        q.normal_()
+        k.normal_()
+        yq = torch.empty((bq, 2048, 2048), device="cuda")
+        fn = lambda: api.qk_softmax(q, k, yq, 128 ** -0.5)  # noqa: E731
+    sec = time_device(torch, fn, args.warmup, args.steps, None, 1)
+    print(json.dumps({"case": c, "size": sz, "ms_per_launch": sec * 1e3}), flush=True)
+
+
 def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     out = {}
     steps, warm = args.steps, args.warmup
@@ -372,7 +430,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     yq = torch.empty((bq, s, s), device="cuda")
     sec = time_device(torch, lambda: api.qk_softmax(q, k, yq, d ** -0.5), warm, steps, dist, world)
     alg = 2 * bq * s * d * 2 + bq * s * s * 4
-    rec("qk_softmax", sec, alg, "GB/s", "hbm", peaks["hbm_gbs"], 2,
+    rec("qk_softmax", sec, alg, "GB/s", "hbm", peaks["hbm_gbs"], 1,
         {"tflops": 2.0 * bq * s * s * d / sec / 1e12})
     del q, k, yq
     torch.cuda.empty_cache()

@@ -22,6 +22,11 @@ inline cudaStream_t asStream(void* s) { return reinterpret_cast<cudaStream_t>(s)
 // Number of SMs of the current device (cached per device).
 int smCount();
 
+// The current device's status word (device memory, allocated once per
+// device): kernels whose bounded waits give up store MLKB_ERR_TIMEOUT there;
+// mlkb_take_device_error() reads and clears it. nullptr if allocation failed.
+int* deviceStatusPtr();
+
 // Launch-check helper: maps a launch error to MLKB_ERR_LAUNCH.
 inline int checkLaunch(const char* what) {
     const cudaError_t e = cudaGetLastError();

@@ -27,9 +27,6 @@
 #include "tc_common.cuh"
 
 namespace mlkb {
-
-__device__ int g_device_status = 0;
-
 namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
@@ -77,7 +74,7 @@ template <bool kBKMajor>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_f16_tcgen05(const __grid_constant__ CUtensorMap tma_a,
                  const __grid_constant__ CUtensorMap tma_b, float* __restrict__ c, int batch,
-                 int m, int n, int k, int accumulate, float scale) {
+                 int m, int n, int k, int accumulate, float scale, int* __restrict__ status) {
     extern __shared__ uint8_t smem_raw[];
     GemmSmem& s = *reinterpret_cast<GemmSmem*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -225,7 +222,7 @@ gemm_f16_tcgen05(const __grid_constant__ CUtensorMap tma_a,
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, 512);
     }
-    if (threadIdx.x == 0 && s.abort) atomicExch(&g_device_status, MLKB_ERR_TIMEOUT);
+    if (threadIdx.x == 0 && s.abort && status != nullptr) atomicExch(status, MLKB_ERR_TIMEOUT);
 }
 
 // Generic SIMT fallback for shapes or alignments TMA cannot take
@@ -279,16 +276,6 @@ int makeTmapF16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, 
 
 }  // namespace mlkb
 
-extern "C" int mlkb_take_device_error(void) {
-    int v = 0;
-    if (cudaMemcpyFromSymbol(&v, mlkb::g_device_status, sizeof(int)) != cudaSuccess) {
-        return mlkb::setCudaError(MLKB_ERR_LAUNCH, cudaGetLastError(), "device status read");
-    }
-    const int zero = 0;
-    cudaMemcpyToSymbol(mlkb::g_device_status, &zero, sizeof(int));
-    return v;
-}
-
 namespace mlkb {
 
 // Launches the tcgen05 GEMM. b_kmajor: B is [batch*n, k] row-major; else [k, n].
@@ -320,11 +307,11 @@ int launchGemmTc(const void* a, const void* b, float* c, int64_t batch, int64_t 
     if (b_kmajor) {
         gemm_f16_tcgen05<true><<<grid, kThreads, kSmemBytes, s>>>(
             ta, tb, c, static_cast<int>(batch), static_cast<int>(m), static_cast<int>(n),
-            static_cast<int>(k), accumulate, scale);
+            static_cast<int>(k), accumulate, scale, deviceStatusPtr());
     } else {
         gemm_f16_tcgen05<false><<<grid, kThreads, kSmemBytes, s>>>(
             ta, tb, c, static_cast<int>(batch), static_cast<int>(m), static_cast<int>(n),
-            static_cast<int>(k), accumulate, scale);
+            static_cast<int>(k), accumulate, scale, deviceStatusPtr());
     }
     return checkLaunch("gemm tcgen05 launch");
 }

@@ -24,61 +24,129 @@ namespace mlkb {
 namespace {
 
 constexpr int kMapThreads = 256;
-constexpr int kMapUnroll = 4;  // float4 vectors per thread per iteration
+constexpr int kMapUnroll = 2;  // float4 vectors per thread per step (plus a prefetched step)
 
+// Near-minimax polynomials on |r| <= pi/4 (fitted for this library by
+// weighted least squares on Chebyshev nodes): sin r = r + r^3 P(r^2) with
+// relative error < 6e-12, cos r = 1 + r^2 Q(r^2) with relative error < 7e-11
+// -- both far below f32 resolution (6e-8), which is all the f32-output
+// kernels need. cos(0) = 1 and sin(r) = r for tiny r hold exactly.
+__device__ __forceinline__ double sin_r(double r, double z) {
+    double p = 2.717971090539634e-06;
+    p = fma(z, p, -0.00019839296518744639);
+    p = fma(z, p, 0.008333329256008314);
+    p = fma(z, p, -0.16666666640376984);
+    return fma(r * z, p, r);
+}
+
+__device__ __forceinline__ double cos_r(double z) {
+    double p = 2.438187363435297e-05;
+    p = fma(z, p, -0.001388666363114334);
+    p = fma(z, p, 0.041666619786184696);
+    p = fma(z, p, -0.49999999689413566);
+    return fma(z, p, 1.0);
+}
+
+// u = fl64(x*x + 3x), exactly the reference chain's value: x*x and 3x are
+// exact in f64 for an f32 x, so one FMA reproduces the Add's single rounding.
 __device__ __forceinline__ double u_of(float x) {
     const double xd = static_cast<double>(x);
     return fma(3.0, xd, xd * xd);
 }
 
+// |x| < 1000 keeps |u| < 2^20, the range of the two-term reduction.
+__device__ __forceinline__ bool fast_range(float4 v) {
+    const uint32_t a = __float_as_uint(v.x) & 0x7fffffffu, b = __float_as_uint(v.y) & 0x7fffffffu;
+    const uint32_t c = __float_as_uint(v.z) & 0x7fffffffu, d = __float_as_uint(v.w) & 0x7fffffffu;
+    return max(max(a, b), max(c, d)) < 0x447a0000u;  // 1000.0f
+}
+
 struct SinOp {
     static constexpr int kOuts = 1;
-    __device__ __forceinline__ static void eval(float x, float* o) {
-        o[0] = static_cast<float>(dev::sin_f64(u_of(x)));
+    __device__ __forceinline__ static void fast(float x, float& y0, float&) {
+        int q;
+        const double r = dev::reduce_pio2(u_of(x), q);
+        const double z = r * r;
+        const double v = (q & 1) ? cos_r(z) : sin_r(r, z);
+        y0 = static_cast<float>((q & 2) ? -v : v);
+    }
+    __device__ __noinline__ static float2 slow(float x) {
+        return make_float2(static_cast<float>(dev::sin_f64(u_of(x))), 0.0f);
     }
 };
 
 struct SinDsinOp {
     static constexpr int kOuts = 2;
-    __device__ __forceinline__ static void eval(float x, float* o) {
+    __device__ __forceinline__ static void fast(float x, float& y0, float& y1) {
+        int q;
+        const double r = dev::reduce_pio2(u_of(x), q);
+        const double z = r * r;
+        const double sr = sin_r(r, z), cr = cos_r(z);
+        // quadrant q: (sin u, cos u) = (sr, cr), (cr, -sr), (-sr, -cr), (-cr, sr)
+        double a = (q & 1) ? cr : sr;
+        double b = (q & 1) ? sr : cr;
+        a = (q & 2) ? -a : a;
+        const double g = fma(2.0, static_cast<double>(x), 3.0);  // 2x + 3, exact
+        const double gs = ((q + 1) & 2) ? -g : g;
+        y0 = static_cast<float>(a);
+        y1 = static_cast<float>(b * gs);
+    }
+    __device__ __noinline__ static float2 slow(float x) {
         double s, c;
         dev::sincos_f64(u_of(x), s, c);
-        const double g = fma(2.0, static_cast<double>(x), 3.0);  // exact
-        o[0] = static_cast<float>(s);
-        o[1] = static_cast<float>(c * g);
+        return make_float2(static_cast<float>(s),
+                           static_cast<float>(c * fma(2.0, static_cast<double>(x), 3.0)));
     }
 };
 
-// Vector body: each thread streams kMapUnroll float4 per iteration (all
-// loads issued before any compute, for memory-level parallelism); the grid
-// strides over the vector range. 16-byte aligned pointers only.
+template <class Op>
+__device__ __forceinline__ void eval4(float4 v, float4& o0, float4& o1) {
+    if (fast_range(v)) {
+        Op::fast(v.x, o0.x, o1.x);
+        Op::fast(v.y, o0.y, o1.y);
+        Op::fast(v.z, o0.z, o1.z);
+        Op::fast(v.w, o0.w, o1.w);
+    } else {  // NaN, inf or |x| >= 1000 somewhere in the vector
+        const float2 a = Op::slow(v.x), b = Op::slow(v.y), c = Op::slow(v.z), d = Op::slow(v.w);
+        o0 = make_float4(a.x, b.x, c.x, d.x);
+        o1 = make_float4(a.y, b.y, c.y, d.y);
+    }
+}
+
+// Vector body: each CTA strides over blocks of kMapThreads*kMapUnroll
+// float4; each thread keeps the next block's loads in flight while it
+// computes the current one. 16-byte aligned pointers only.
 template <class Op>
 __global__ void __launch_bounds__(kMapThreads)
 map_vec_kernel(const float4* __restrict__ x, float4* __restrict__ y0,
                float4* __restrict__ y1, int64_t nvec) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * kMapThreads * kMapUnroll;
-    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kMapThreads * kMapUnroll +
-                        threadIdx.x;
-         base < nvec; base += stride) {
-        float4 v[kMapUnroll];
+    constexpr int64_t kBlock = static_cast<int64_t>(kMapThreads) * kMapUnroll;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kBlock;
+    int64_t base = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    float4 cur[kMapUnroll];
+#pragma unroll
+    for (int u = 0; u < kMapUnroll; ++u) {
+        const int64_t i = base + u * kMapThreads;
+        if (i < nvec) cur[u] = __ldcs(x + i);
+    }
+    for (; base < nvec; base += stride) {
+        float4 nxt[kMapUnroll];
+        const int64_t nb = base + stride;
 #pragma unroll
         for (int u = 0; u < kMapUnroll; ++u) {
-            const int64_t i = base + static_cast<int64_t>(u) * kMapThreads;
-            if (i < nvec) v[u] = __ldcs(x + i);
+            const int64_t i = nb + u * kMapThreads;
+            if (i < nvec) nxt[u] = __ldcs(x + i);
         }
 #pragma unroll
         for (int u = 0; u < kMapUnroll; ++u) {
-            const int64_t i = base + static_cast<int64_t>(u) * kMapThreads;
-            if (i >= nvec) break;
-            float o[4][2];
-            Op::eval(v[u].x, o[0]);
-            Op::eval(v[u].y, o[1]);
-            Op::eval(v[u].z, o[2]);
-            Op::eval(v[u].w, o[3]);
-            __stcs(y0 + i, make_float4(o[0][0], o[1][0], o[2][0], o[3][0]));
-            if (Op::kOuts > 1) {
-                __stcs(y1 + i, make_float4(o[0][1], o[1][1], o[2][1], o[3][1]));
+            const int64_t i = base + u * kMapThreads;
+            if (i < nvec) {
+                float4 o0, o1;
+                eval4<Op>(cur[u], o0, o1);
+                __stcs(y0 + i, o0);
+                if (Op::kOuts > 1) __stcs(y1 + i, o1);
             }
+            cur[u] = nxt[u];
         }
     }
 }
@@ -90,10 +158,9 @@ __global__ void map_scalar_kernel(const float* __restrict__ x, float* __restrict
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t i = begin + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
          i < n; i += stride) {
-        float o[2];
-        Op::eval(x[i], o);
-        y0[i] = o[0];
-        if (Op::kOuts > 1) y1[i] = o[1];
+        const float2 o = Op::slow(x[i]);
+        y0[i] = o.x;
+        if (Op::kOuts > 1) y1[i] = o.y;
     }
 }
 
@@ -106,10 +173,10 @@ int gridFor(int64_t work, int per_block) {
 template <class Op>
 int launchMap(const float* x, float* y0, float* y1, int64_t n, void* stream) {
     if (n < 0) return setError(MLKB_ERR_INVALID, "map: negative element count");
+    if (n == 0) return okStatus();
     if (x == nullptr || y0 == nullptr || (Op::kOuts > 1 && y1 == nullptr)) {
         return setError(MLKB_ERR_INVALID, "map: null buffer");
     }
-    if (n == 0) return okStatus();
     cudaStream_t s = asStream(stream);
     const bool vec = aligned16(x) && aligned16(y0) && (Op::kOuts < 2 || aligned16(y1));
     int64_t done = 0;
@@ -282,6 +349,7 @@ extern "C" int mlkb_map_chain(const mlkb_expr* exprs, int32_t n_exprs, int32_t p
                               void* stream) {
     using namespace mlkb;
     if (n < 0) return setError(MLKB_ERR_INVALID, "chain: negative element count");
+    if (n == 0) return okStatus();
     if (out == nullptr) return setError(MLKB_ERR_INVALID, "chain: null output");
     if (int st = checkChain(exprs, n_exprs, b != nullptr)) return st;
     if (elem_dtype != MLKB_F32 && elem_dtype != MLKB_F64) {

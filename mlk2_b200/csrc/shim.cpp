@@ -61,6 +61,23 @@ int smCount() {
     return cache[dev];
 }
 
+int* deviceStatusPtr() {
+    static int* words[64] = {nullptr};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (words[dev] == nullptr) {
+        int* p = nullptr;
+        if (cudaMalloc(&p, 16) != cudaSuccess || cudaMemset(p, 0, 16) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        words[dev] = p;
+    }
+    return words[dev];
+}
+
 namespace {
 
 int elemBytes(int dtype) {
@@ -497,6 +514,18 @@ extern "C" const char* mlkb_last_error(void) { return t_err.c_str(); }
 extern "C" int mlk_last_status(void) { return t_status; }
 extern "C" const char* mlkb_version(void) { return "mlkb200 0.1.0 sm_100a"; }
 extern "C" int mlkb_device_count(void) { return deviceCount(); }
+
+extern "C" int mlkb_take_device_error(void) {
+    if (deviceCount() <= 0) return setError(MLKB_ERR_NO_DEVICE, "no CUDA device");
+    int* p = deviceStatusPtr();
+    if (p == nullptr) return setError(MLKB_ERR_CUDA_MEM, "device status word unavailable");
+    int v = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, sizeof(int));
+    if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "device status read");
+    return v;
+}
 
 extern "C" int mlkb_module_create(const char* json, mlkb_module** out) {
     if (out == nullptr) return setError(MLKB_ERR_INVALID, "module_create: null out");

@@ -13,6 +13,7 @@
 // float4-aligned) take a three-pass streaming kernel with the same
 // arithmetic.
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace mlkb {
 namespace {
@@ -60,59 +61,166 @@ __device__ __forceinline__ double blockSum(double v, double* sm) {
     return r;
 }
 
-// Register-resident row softmax: thread t owns float4 vectors t + 256*j,
-// j < NV, of its row (cols <= 1024*NV, cols % 4 == 0, 16-byte aligned rows).
-template <int NV>
+// 2^(j/64), j = 0..63, correctly rounded f64.
+__device__ const double kExp2Tab[64] = {
+    1.0, 1.0108892860517005, 1.0218971486541166, 1.0330248790212284,
+    1.0442737824274138, 1.0556451783605572, 1.0671404006768237, 1.0787607977571199,
+    1.0905077326652577, 1.102382583307841, 1.1143867425958924, 1.1265216186082418,
+    1.1387886347566916, 1.1511892299529827, 1.1637248587775775, 1.1763969916502812,
+    1.189207115002721, 1.202156731452703, 1.215247359980469, 1.22848053610687,
+    1.241857812073484, 1.255380757024691, 1.2690509571917332, 1.2828700160787783,
+    1.2968395546510096, 1.3109612115247644, 1.3252366431597413, 1.339667524053303,
+    1.3542555469368927, 1.3690024229745905, 1.383909881963832, 1.3989796725383112,
+    1.4142135623730951, 1.42961333839197, 1.4451808069770467, 1.460917794180647,
+    1.4768261459394993, 1.4929077282912648, 1.5091644275934228, 1.5255981507445384,
+    1.5422108254079407, 1.559004400237837, 1.5759808451078865, 1.593142151342267,
+    1.6104903319492543, 1.6280274218573478, 1.645755478153965, 1.6636765803267364,
+    1.681792830507429, 1.7001063537185235, 1.718619298122478, 1.7373338352737062,
+    1.7562521603732995, 1.7753764925265212, 1.7947090750031072, 1.8142521755003989,
+    1.8340080864093424, 1.8539791250833855, 1.8741676341103, 1.8945759815869656,
+    1.9152065613971474, 1.9360617934922943, 1.9571441241754002, 1.978456026387951,
+};
+
+// exp(d) in f64 for d <= 0: k = rint(64 d / ln2), r = d - k ln2/64 (two-term
+// constant; the first product is exact under FMA), |r| <= ln2/128, so a cubic
+// in r has relative error < 4e-11; then 2^(k/64) = 2^(k>>6) * T[k&63] with the
+// power of two added to T's exponent field. d < -120 gives 0 (such terms are
+// below half the smallest f32 subnormal relative to any row sum >= 1 and add
+// nothing to it); NaN propagates; -inf gives 0.
+__device__ __forceinline__ double exp_neg_tab(double d, const double* tab) {
+    // Branch-free: every lane evaluates the formula (the table index k & 63 is
+    // always in range), then out-of-range lanes take 0 or their NaN.
+    const double kMagic = 6755399441055744.0;
+    const double t = fma(d, 92.33248261689366, kMagic);
+    const double kd = t - kMagic;
+    const int k = __double2loint(t);
+    double r = fma(-kd, 0.010830424696249145, d);
+    r = fma(-kd, 3.623510646634843e-19, r);
+    double p = fma(r, 0.16666666666666666, 0.5);
+    p = fma(p, r, 1.0);
+    p = fma(p, r, 1.0);
+    const double tj = tab[k & 63];
+    const double scale = __hiloint2double(__double2hiint(tj) + ((k >> 6) << 20),
+                                          __double2loint(tj));
+    const double e = p * scale;
+    return (d >= -120.0) ? e : ((d != d) ? d : 0.0);
+}
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(tc::smem_u32(smem_dst)), "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+        : "memory");
+}
+
+constexpr uint64_t kRowWaitLimitNs = 2000000000ull;
+
+// Row softmax, persistent CTAs: each CTA owns rows blockIdx.x + i*gridDim.x.
+// A TMA bulk copy brings row i+2 into a shared-memory double buffer while row
+// i is computed, so HBM reads stay in flight across the block reductions.
+// Thread t owns float4 vectors t + 256*j (j < NV) of its row; exponentials
+// are kept in registers between the sum and the write (read once, write
+// once). cols % 4 == 0, cols <= 1024*NV, 16-byte aligned rows.
+template <int NV, bool kFull>
 __global__ void __launch_bounds__(kRowThreads)
-softmax_rows_reg(const float* __restrict__ x, float* __restrict__ y, int64_t rows,
-                 int64_t cols) {
+softmax_rows_tma(const float* __restrict__ x, float* __restrict__ y, int64_t rows,
+                 int64_t cols, int* __restrict__ status) {
+    extern __shared__ __align__(128) uint8_t dyn[];
+    __shared__ uint64_t full[2];
+    __shared__ double tab[64];
     __shared__ float smax[kRowWarps];
     __shared__ double ssum[kRowWarps];
-    const int64_t nvec = cols >> 2;
-    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-        const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
-        float4* yr = reinterpret_cast<float4*>(y + row * cols);
+    const uint32_t row_bytes = static_cast<uint32_t>(cols) * 4u;
+    const uint32_t buf_bytes = (row_bytes + 127u) & ~127u;
+    const int nvec = static_cast<int>(cols >> 2);
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        tc::mbar_init(&full[0], 1);
+        tc::mbar_init(&full[1], 1);
+        tc::fence_barrier_init();
+    }
+    if (tid < 64) tab[tid] = kExp2Tab[tid];
+    __syncthreads();
+    if (tid == 0) {
+        for (int b = 0; b < 2; ++b) {
+            const int64_t r = blockIdx.x + static_cast<int64_t>(b) * gridDim.x;
+            if (r < rows) {
+                tc::mbar_arrive_expect_tx(&full[b], row_bytes);
+                bulk_load(dyn + b * buf_bytes, x + r * cols, row_bytes, &full[b]);
+            }
+        }
+    }
+    int it = 0;
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
+        const int b = it & 1;
+        int never = 0;
+        const bool ok = tc::mbar_wait(&full[b], (it >> 1) & 1, &never, kRowWaitLimitNs);
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0 && status != nullptr) atomicExch(status, MLKB_ERR_TIMEOUT);
+            break;
+        }
+        const float4* xr = reinterpret_cast<const float4*>(dyn + b * buf_bytes);
         float4 v[NV];
         float m = -INFINITY;
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            const int64_t c = threadIdx.x + static_cast<int64_t>(j) * kRowThreads;
-            if (c < nvec) {
-                v[j] = __ldcs(xr + c);
+            const int c = tid + j * kRowThreads;
+            if (kFull || c < nvec) {
+                v[j] = xr[c];
                 m = (v[j].x > m) ? v[j].x : m;
                 m = (v[j].y > m) ? v[j].y : m;
                 m = (v[j].z > m) ? v[j].z : m;
                 m = (v[j].w > m) ? v[j].w : m;
             }
         }
-        m = blockMax(m, smax);
+        m = blockMax(m, smax);  // every thread has read buffer b past this barrier
+        if (tid == 0) {
+            const int64_t nxt = row + 2 * static_cast<int64_t>(gridDim.x);
+            if (nxt < rows) {
+                tc::fence_proxy_async();
+                tc::mbar_arrive_expect_tx(&full[b], row_bytes);
+                bulk_load(dyn + b * buf_bytes, x + nxt * cols, row_bytes, &full[b]);
+            }
+        }
         const double md = static_cast<double>(m);
         double e[NV][4];
         double s = 0.0;
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            const int64_t c = threadIdx.x + static_cast<int64_t>(j) * kRowThreads;
-            if (c < nvec) {
-                e[j][0] = dev::exp_neg_f64(static_cast<double>(v[j].x) - md);
-                e[j][1] = dev::exp_neg_f64(static_cast<double>(v[j].y) - md);
-                e[j][2] = dev::exp_neg_f64(static_cast<double>(v[j].z) - md);
-                e[j][3] = dev::exp_neg_f64(static_cast<double>(v[j].w) - md);
+            const int c = tid + j * kRowThreads;
+            if (kFull || c < nvec) {
+                e[j][0] = exp_neg_tab(static_cast<double>(v[j].x) - md, tab);
+                e[j][1] = exp_neg_tab(static_cast<double>(v[j].y) - md, tab);
+                e[j][2] = exp_neg_tab(static_cast<double>(v[j].z) - md, tab);
+                e[j][3] = exp_neg_tab(static_cast<double>(v[j].w) - md, tab);
                 s += (e[j][0] + e[j][1]) + (e[j][2] + e[j][3]);
             }
         }
         s = blockSum(s, ssum);
         const bool nz = (s != 0.0);
         const double inv = nz ? 1.0 / s : 0.0;
+        float4* yr = reinterpret_cast<float4*>(y + row * cols);
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            const int64_t c = threadIdx.x + static_cast<int64_t>(j) * kRowThreads;
-            if (c < nvec) {
+            const int c = tid + j * kRowThreads;
+            if (kFull || c < nvec) {
                 float4 o;
                 o.x = nz ? static_cast<float>(e[j][0] * inv) : 0.0f;
                 o.y = nz ? static_cast<float>(e[j][1] * inv) : 0.0f;
                 o.z = nz ? static_cast<float>(e[j][2] * inv) : 0.0f;
                 o.w = nz ? static_cast<float>(e[j][3] * inv) : 0.0f;
                 __stcs(yr + c, o);
+            }
+        }
+    }
+    // Drain: a prefetch that was issued is complete before the CTA exits.
+    if (tid == 0) {
+        for (int j = it; j < it + 2; ++j) {
+            const int64_t r = blockIdx.x + static_cast<int64_t>(j) * gridDim.x;
+            if (r < rows) {
+                int never = 0;
+                (void)tc::mbar_wait(&full[j & 1], (j >> 1) & 1, &never, kRowWaitLimitNs);
             }
         }
     }
@@ -211,23 +319,49 @@ int checkRows(const void* x, const void* y, int64_t rows, int64_t cols) {
 }  // namespace
 }  // namespace mlkb
 
+namespace mlkb {
+namespace {
+
+template <int NV, bool kFull>
+int launchRowsTma(const float* x, float* y, int64_t rows, int64_t cols, cudaStream_t s) {
+    const uint32_t buf = ((static_cast<uint32_t>(cols) * 4u + 127u) & ~127u);
+    const size_t smem = 2 * static_cast<size_t>(buf);
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(softmax_rows_tma<NV, kFull>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   64 * 1024);
+        if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "softmax smem attribute");
+        attr[dev] = true;
+    }
+    const int per_sm = NV <= 2 ? 6 : NV <= 4 ? 4 : 2;
+    softmax_rows_tma<NV, kFull><<<rowGrid(rows, per_sm), kRowThreads, smem, s>>>(
+        x, y, rows, cols, deviceStatusPtr());
+    return checkLaunch("softmax launch");
+}
+
+template <int NV>
+int launchRows(const float* x, float* y, int64_t rows, int64_t cols, cudaStream_t s) {
+    return cols == NV * 4 * kRowThreads ? launchRowsTma<NV, true>(x, y, rows, cols, s)
+                                        : launchRowsTma<NV, false>(x, y, rows, cols, s);
+}
+
+}  // namespace
+}  // namespace mlkb
+
 extern "C" int mlkb_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols,
                                 void* stream) {
     using namespace mlkb;
     if (int st = checkRows(x, y, rows, cols)) return st;
     cudaStream_t s = asStream(stream);
     const bool vec = (cols % 4 == 0) && aligned16(x) && aligned16(y);
-    if (vec && cols <= 1024) {
-        softmax_rows_reg<1><<<rowGrid(rows, 8), kRowThreads, 0, s>>>(x, y, rows, cols);
-    } else if (vec && cols <= 2048) {
-        softmax_rows_reg<2><<<rowGrid(rows, 8), kRowThreads, 0, s>>>(x, y, rows, cols);
-    } else if (vec && cols <= 4096) {
-        softmax_rows_reg<4><<<rowGrid(rows, 8), kRowThreads, 0, s>>>(x, y, rows, cols);
-    } else if (vec && cols <= 8192) {
-        softmax_rows_reg<8><<<rowGrid(rows, 4), kRowThreads, 0, s>>>(x, y, rows, cols);
-    } else {
-        softmax_rows_stream<float><<<rowGrid(rows, 8), kRowThreads, 0, s>>>(x, y, rows, cols);
-    }
+    if (vec && cols <= 1024) return launchRows<1>(x, y, rows, cols, s);
+    if (vec && cols <= 2048) return launchRows<2>(x, y, rows, cols, s);
+    if (vec && cols <= 4096) return launchRows<4>(x, y, rows, cols, s);
+    if (vec && cols <= 8192) return launchRows<8>(x, y, rows, cols, s);
+    softmax_rows_stream<float><<<rowGrid(rows, 8), kRowThreads, 0, s>>>(x, y, rows, cols);
     return checkLaunch("softmax launch");
 }
 

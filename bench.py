@@ -222,8 +222,6 @@ def main():
         run_reference_arm(args, rank)
         return
 
-    import datetime
-
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -231,10 +229,11 @@ def main():
     import mlk2_b200 as mb
     from mlk2_b200 import api, kir
 
+    from mlk2_b200 import dist as mdist
+
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        mdist.init("nccl", local, timeout_s=120.0)
     peaks = load_peaks()
     traffic = load_traffic()
 
@@ -256,6 +255,28 @@ def main():
                 "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
                 "kernel": "map_vec_kernel<SinDsinOp>",
                 "traffic": traffic.get("map2", {}).get("bytes_per_launch")}
+
+    # ---- optional assembly of the sharded result (the only collective) ----------
+    gather = None
+    if world > 1:
+        for _ in range(2):
+            full = mdist.all_gather_shards(y, dist)
+            del full
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        full = mdist.all_gather_shards(y, dist)
+        g1.record()
+        torch.cuda.synchronize()
+        gms = mdist.max_over_ranks(g0.elapsed_time(g1), dist, device="cuda")
+        out_bytes = full.numel() * 4
+        gather = {"what": "NCCL all_gather_into_tensor of y (f32) onto every rank",
+                  "bytes_out_per_rank": out_bytes, "ms": gms,
+                  "busbw_gbs": out_bytes * (world - 1) / world / (gms / 1e3) / 1e9,
+                  "note": "reported separately; not part of value"}
+        del full
+        torch.cuda.empty_cache()
 
     # ---- e2e through the C-ABI host entry ---------------------------------------
     del y, dy
@@ -310,7 +331,7 @@ def main():
                        "elements_per_gpu": n, "global_elements": n * world,
                        "parallelism": f"dp{world} (contiguous element shards)",
                        "l2": "inputs 1 GiB per GPU > 126 MB L2, no flush"},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gather": gather,
             "gpu_launches": args.steps + sum(c.get("gpu_launches", 0) for c in configs.values()),
             "clocks": clocks, "configs": configs, "library": mb.version(),
         }

@@ -141,6 +141,14 @@ int mlkb_device_count(void);
  * 0 when clear. Synchronises with the device. */
 int mlkb_take_device_error(void);
 
+/* Launches a one-CTA kernel whose mbarrier wait can never complete; the
+ * bounded wait used by every device-side spin in this library gives up after
+ * limit_ns (at most 2 s) and records MLKB_ERR_TIMEOUT, which
+ * mlkb_take_device_error() then returns. Exercises failure detection without
+ * faulting or hanging the GPU. No reference counterpart: the reference never
+ * ran on a device. */
+int mlkb_selftest_bounded_wait(uint64_t limit_ns, void* stream);
+
 /* ======================================================================= */
 /* 2. Module entry points                                                   */
 /* ======================================================================= */

@@ -15,6 +15,7 @@ SIGNATURES = {
     "mlkb_version": (cp, []),
     "mlkb_device_count": (i32, []),
     "mlkb_take_device_error": (i32, []),
+    "mlkb_selftest_bounded_wait": (i32, [u64, vp]),
     "mlkb_module_create": (i32, [cp, C.POINTER(vp)]),
     "mlkb_module_destroy": (None, [vp]),
     "mlkb_module_kind": (i32, [vp]),

@@ -6,22 +6,23 @@
 // Q and K are f16 [batch, s, d] row-major here, so K is already the K-major
 // operand the tcgen05 MMA wants: no transpose is materialised.
 //
-// Fused kernel (s % 256 == 0, d in {64, 128}); one CTA per SM, persistent
+// Fused kernel (s % 128 == 0, d in {64, 128}); one CTA per SM, persistent
 // over units = (batch, 128-row band). The output write (4 B per score) is the
-// roofline, so every score is written exactly once and nothing else is:
-//   warp 0     TMA producer: the Q band [128 x d] once per unit, then K in
-//              [256 x 64] boxes through a 4-stage ring (128 KB in flight covers
-//              the L2 latency at the MMA's consumption rate), all s/256 column
-//              chunks twice (pass 1 and pass 2);
-//   warp 1     MMA issuer: tcgen05.mma M128 N256 K16 (both operands K-major)
-//              into one of two TMEM accumulators per chunk;
-//   warps 2-17 epilogue, four warps per TMEM lane quarter (64 columns each):
-//              pass 1 keeps an online row max / sum of exp2(scale*log2e*s);
-//              the four parts merge their statistics through shared memory;
-//              pass 2 recomputes each chunk (the MMA is far cheaper than a
-//              second trip through HBM) and writes exp2(v - m) / l, transposed
-//              through an XOR-swizzled shared-memory tile so that every global
-//              store is a full 128-byte row segment.
+// roofline, so every score is written exactly once and nothing else is. Each
+// unit needs two passes over its scores (row statistics, then the normalised
+// write); running them back to back would leave HBM idle during the first.
+// Instead the CTA overlaps pass 1 of unit i with pass 2 of unit i-1:
+//   warp 0       TMA producer: Q bands into three slots, K in [128 x 64] boxes
+//                through a 5-stage ring, in the MMA's consumption order;
+//   warp 1       MMA issuer: per 128-column chunk, tcgen05.mma M128 N128 K16
+//                (both operands K-major) for pass 2 of unit i-1 and pass 1 of
+//                unit i, into four 128-column TMEM accumulators (two per pass);
+//   warps 2-9    group A (pass 1), two warps per TMEM lane quarter: online row
+//                max / sum of exp2(scale*log2e*s), handed to group B through a
+//                double-buffered statistics slot;
+//   warps 10-17  group B (pass 2): recompute, normalise, transpose through an
+//                XOR-swizzled shared-memory tile so every global store is a
+//                full 128-byte row segment.
 // Every mbarrier wait is bounded (2 s); on a timeout the CTA raises the
 // device status word, drains its copies, frees TMEM and returns.
 // Other shapes use the two-step form (tcgen05 GEMM with the scale folded into
@@ -42,25 +43,26 @@ int makeTmapF16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, 
 
 namespace {
 
-constexpr int kRows = 128;          // score rows per unit (M of the MMA)
-constexpr int kChunk = 256;         // score columns per accumulator (N of the MMA)
-constexpr int kKStages = 4;         // K ring depth, [256 x 64] f16 boxes
-constexpr uint32_t kKBox = kChunk * 64 * 2;   // 32 KB
-constexpr uint32_t kQBox = kRows * 64 * 2;    // 16 KB
-constexpr int kEpiWarps = 16;                 // 4 per TMEM lane quarter
-constexpr int kParts = kEpiWarps / 4;         // column parts of a chunk
-constexpr int kPartCols = kChunk / kParts;    // 64 columns per warp per chunk
-constexpr int kThreads = 64 + kEpiWarps * 32;  // 576
-constexpr uint32_t kStageTile = 32 * 32 * 4;  // [32 rows x 32 cols] f32 = 4 KB
+constexpr int kRows = 128;   // score rows per unit (M of the MMA)
+constexpr int kChunk = 128;  // score columns per accumulator (N of the MMA)
+constexpr int kKStages = 5;  // K ring depth, [128 x 64] f16 boxes
+constexpr int kQSlots = 3;   // Q bands resident: units i-1, i and the prefetched i+1
+constexpr uint32_t kKBox = kChunk * 64 * 2;  // 16 KB
+constexpr uint32_t kQBox = kRows * 64 * 2;   // 16 KB (one d-half)
+constexpr int kGroupWarps = 8;               // per epilogue group, 2 per lane quarter
+constexpr int kThreads = 64 + 2 * kGroupWarps * 32;  // 576
+constexpr uint32_t kStageTile = 32 * 32 * 4;         // [32 rows x 32 cols] f32
 constexpr uint64_t kLimitNs = 2000000000ull;
 
 struct QkSmem {
-    uint8_t k[kKStages][kKBox];       // 128 KB
-    uint8_t q[2][kQBox];              // 32 KB (two d-halves)
-    uint8_t out[kEpiWarps][kStageTile];  // 64 KB; also carries the row statistics
+    uint8_t k[kKStages][kKBox];              // 80 KB
+    uint8_t q[kQSlots][2][kQBox];            // 96 KB
+    uint8_t out[kGroupWarps][kStageTile];    // 32 KB (group B staging)
+    float2 stats[2][2][kRows];               // [slot][part][row] = (max, sum)
     uint64_t kfull[kKStages], kempty[kKStages];
-    uint64_t qfull, qempty;
-    uint64_t tfull[2], tempty[2];
+    uint64_t qfull[kQSlots], qempty[kQSlots];
+    uint64_t afull[2], aempty[2], bfull[2], bempty[2];
+    uint64_t sfull[2], sempty[2];
     uint32_t tmem_base;
     int abort;
 };
@@ -73,15 +75,16 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-__device__ __forceinline__ void named_sync(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+// Lane-0 arrive after the whole warp is done with the guarded resource.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(bar);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
 qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
-                   const __grid_constant__ CUtensorMap tma_k,
-                   float* __restrict__ y, int batch, int s, int d, float c2,
-                   uint32_t stagger_ns, int* __restrict__ status) {
+                   const __grid_constant__ CUtensorMap tma_k, float* __restrict__ y, int batch,
+                   int s, int d, float c2, int* __restrict__ status) {
     // The kernel has no static shared memory, so the dynamic window starts at
     // the 1024-byte aligned base the 128B-swizzled tiles need.
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -94,18 +97,28 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
     const int bands = s / kRows;
     const int units = batch * bands;
     const int chunks = s / kChunk;
-    const int dh = d / 64;  // d-halves per chunk (1 or 2)
+    const int dh = d / 64;  // d-halves (1 or 2)
+    // this CTA's units: blockIdx.x + i*gridDim.x, i < n
+    const int n = units > static_cast<int>(blockIdx.x)
+                      ? (units - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                      : 0;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kKStages; ++i) {
             tc::mbar_init(&sm.kfull[i], 1);
             tc::mbar_init(&sm.kempty[i], 1);
         }
-        tc::mbar_init(&sm.qfull, 1);
-        tc::mbar_init(&sm.qempty, 1);
+        for (int i = 0; i < kQSlots; ++i) {
+            tc::mbar_init(&sm.qfull[i], 1);
+            tc::mbar_init(&sm.qempty[i], 1);
+        }
         for (int i = 0; i < 2; ++i) {
-            tc::mbar_init(&sm.tfull[i], 1);
-            tc::mbar_init(&sm.tempty[i], kEpiWarps);
+            tc::mbar_init(&sm.afull[i], 1);
+            tc::mbar_init(&sm.aempty[i], kGroupWarps);
+            tc::mbar_init(&sm.bfull[i], 1);
+            tc::mbar_init(&sm.bempty[i], kGroupWarps);
+            tc::mbar_init(&sm.sfull[i], kGroupWarps);
+            tc::mbar_init(&sm.sempty[i], kGroupWarps);
         }
         sm.abort = 0;
         tc::fence_barrier_init();
@@ -117,40 +130,56 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
     tc::tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
     volatile int* abort = &sm.abort;
-
-    // Pass 1 only computes and pass 2 mostly writes; CTAs that start together
-    // would alternate between an idle and an oversubscribed HBM. Odd CTAs start
-    // about one pass late, so at any time half the SMs are writing.
-    if ((blockIdx.x & 1) && stagger_ns > 0 && warp == 0 && lane == 0) {
-        const uint64_t t0 = tc::global_timer_ns();
-        while (tc::global_timer_ns() - t0 < stagger_ns) __nanosleep(1000);
-    }
+    auto unit_of = [&](int i) {
+        return static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+    };
 
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer ----------------
         tc::prefetch_tmap(&tma_q);
         tc::prefetch_tmap(&tma_k);
-        uint32_t kit = 0, ui = 0;
-        for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x, ++ui) {
+        uint32_t kit = 0;
+        auto load_q = [&](int i) -> bool {
+            const int slot = i % kQSlots;
+            if (i >= kQSlots &&
+                !tc::mbar_wait(&sm.qempty[slot], ((i / kQSlots) - 1) & 1, abort, kLimitNs)) {
+                return false;
+            }
+            const int u = unit_of(i);
             const int b = u / bands, band = u - b * bands;
-            const int qrow = b * s + band * kRows;
-            if (!tc::mbar_wait(&sm.qempty, (ui & 1u) ^ 1u, abort, kLimitNs)) break;
-            tc::mbar_arrive_expect_tx(&sm.qfull, kQBox * dh);
-            for (int h = 0; h < dh; ++h) tc::tma_load_2d(sm.q[h], &tma_q, &sm.qfull, h * 64, qrow);
-            for (int c = 0; c < 2 * chunks; ++c) {
-                const int krow = b * s + (c % chunks) * kChunk;
-                for (int h = 0; h < dh; ++h, ++kit) {
-                    const int st = static_cast<int>(kit % kKStages);
-                    if (!tc::mbar_wait(&sm.kempty[st], ((kit / kKStages) & 1u) ^ 1u, abort,
-                                       kLimitNs)) {
-                        goto producer_done;
-                    }
-                    tc::mbar_arrive_expect_tx(&sm.kfull[st], kKBox);
-                    tc::tma_load_2d(sm.k[st], &tma_k, &sm.kfull[st], h * 64, krow);
+            tc::mbar_arrive_expect_tx(&sm.qfull[slot], kQBox * dh);
+            for (int h = 0; h < dh; ++h) {
+                tc::tma_load_2d(sm.q[slot][h], &tma_q, &sm.qfull[slot], h * 64,
+                                b * s + band * kRows);
+            }
+            return true;
+        };
+        auto load_k = [&](int i, int c) -> bool {
+            const int b = unit_of(i) / bands;
+            for (int h = 0; h < dh; ++h, ++kit) {
+                const int st = static_cast<int>(kit % kKStages);
+                if (!tc::mbar_wait(&sm.kempty[st], ((kit / kKStages) & 1u) ^ 1u, abort,
+                                   kLimitNs)) {
+                    return false;
                 }
+                tc::mbar_arrive_expect_tx(&sm.kfull[st], kKBox);
+                tc::tma_load_2d(sm.k[st], &tma_k, &sm.kfull[st], h * 64, b * s + c * kChunk);
+            }
+            return true;
+        };
+        bool ok = true;
+        for (int i = 0; i < n && i < 2 && ok; ++i) ok = load_q(i);
+        // Q of unit step+1 reuses the slot of unit step-2, free once the MMA has
+        // finished step-1; a chunk into this step that is the case, and the
+        // band still lands a whole step before it is needed.
+        const int qload_at = chunks > 1 ? 1 : 0;
+        for (int step = 0; step <= n && ok; ++step) {
+            for (int c = 0; c < chunks && ok; ++c) {
+                if (step > 0) ok = load_k(step - 1, c);   // pass 2 of unit step-1
+                if (ok && step < n) ok = load_k(step, c);  // pass 1 of unit step
+                if (ok && c == qload_at && step + 1 < n && step + 1 >= 2) ok = load_q(step + 1);
             }
         }
-    producer_done:
         for (uint32_t j = kit > kKStages ? kit - kKStages : 0; j < kit; ++j) {
             int never = 0;
             (void)tc::mbar_wait(&sm.kfull[j % kKStages], (j / kKStages) & 1u, &never, kLimitNs);
@@ -158,112 +187,136 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer ----------------
         constexpr uint32_t kIdesc = tc::idesc_f16_f32(kRows, kChunk, 0, 0);
-        uint32_t kit = 0, acc_it = 0, ui = 0;
-        for (int u = blockIdx.x; u < units; u += gridDim.x, ++ui) {
-            if (!tc::mbar_wait(&sm.qfull, ui & 1u, abort, kLimitNs)) goto mma_done;
-            tc::tc_fence_after();
-            for (int c = 0; c < 2 * chunks; ++c, ++acc_it) {
-                const uint32_t acc = acc_it & 1u;
-                if (!tc::mbar_wait(&sm.tempty[acc], ((acc_it >> 1) & 1u) ^ 1u, abort, kLimitNs)) {
-                    goto mma_done;
+        uint32_t kit = 0, ait = 0, bit = 0;
+        // One accumulator chunk: Q slot x K chunk -> TMEM columns `dst`.
+        auto mma_chunk = [&](int qslot, uint32_t dst) -> bool {
+            for (int h = 0; h < dh; ++h, ++kit) {
+                const int st = static_cast<int>(kit % kKStages);
+                if (!tc::mbar_wait(&sm.kfull[st], (kit / kKStages) & 1u, abort, kLimitNs)) {
+                    return false;
                 }
                 tc::tc_fence_after();
-                const uint32_t dst = tmem + acc * kChunk;
-                for (int h = 0; h < dh; ++h, ++kit) {
-                    const int st = static_cast<int>(kit % kKStages);
-                    if (!tc::mbar_wait(&sm.kfull[st], (kit / kKStages) & 1u, abort, kLimitNs)) {
-                        goto mma_done;
-                    }
-                    tc::tc_fence_after();
-                    const uint32_t q0 = tc::smem_u32(sm.q[h]);
-                    const uint32_t k0 = tc::smem_u32(sm.k[st]);
+                const uint32_t q0 = tc::smem_u32(sm.q[qslot][h]);
+                const uint32_t k0 = tc::smem_u32(sm.k[st]);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        tc::mma_f16(dst, tc::smem_desc_sw128(q0 + kk * 32, 16, 1024),
-                                    tc::smem_desc_sw128(k0 + kk * 32, 16, 1024), kIdesc,
-                                    (h > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    tc::mma_commit(&sm.kempty[st]);
+                for (int kk = 0; kk < 4; ++kk) {
+                    tc::mma_f16(dst, tc::smem_desc_sw128(q0 + kk * 32, 16, 1024),
+                                tc::smem_desc_sw128(k0 + kk * 32, 16, 1024), kIdesc,
+                                (h > 0 || kk > 0) ? 1u : 0u);
                 }
-                tc::mma_commit(&sm.tfull[acc]);
+                tc::mma_commit(&sm.kempty[st]);
             }
-            tc::mma_commit(&sm.qempty);  // Q band free once this unit's MMAs finish
-        }
-    mma_done:;
-    } else if (warp >= 2) {
-        // ---------------- epilogue ----------------
-        const int ew = warp - 2;            // 0..15
-        const int quarter = warp & 3;       // TMEM lanes this warp may read
-        const int part = ew >> 2;           // which 64 columns of a chunk
-        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-        uint8_t* const tile = sm.out[ew];
-        uint32_t acc_it = 0;
-        for (int u = blockIdx.x; u < units; u += gridDim.x) {
-            const int b = u / bands, band = u - b * bands;
-            const int ybase_row = b * s + band * kRows + quarter * 32;
-            float m = -INFINITY, l = 0.0f;
-            // pass 1: online max / sum over this thread's row, 64 columns per chunk
-            for (int c = 0; c < chunks; ++c, ++acc_it) {
-                const uint32_t acc = acc_it & 1u;
-                if (!tc::mbar_wait(&sm.tfull[acc], (acc_it >> 1) & 1u, abort, kLimitNs)) {
-                    goto epi_done;
+            return true;
+        };
+        for (int step = 0; step <= n; ++step) {
+            if (step < n &&
+                !tc::mbar_wait(&sm.qfull[step % kQSlots], (step / kQSlots) & 1, abort, kLimitNs)) {
+                break;
+            }
+            tc::tc_fence_after();
+            bool ok = true;
+            for (int c = 0; c < chunks && ok; ++c) {
+                if (step > 0) {  // pass 2 of unit step-1 -> accumulators B (256, 384)
+                    const uint32_t acc = bit & 1u;
+                    ok = tc::mbar_wait(&sm.bempty[acc], ((bit >> 1) & 1u) ^ 1u, abort, kLimitNs);
+                    tc::tc_fence_after();
+                    ok = ok && mma_chunk((step - 1) % kQSlots, tmem + 256 + acc * kChunk);
+                    if (ok) tc::mma_commit(&sm.bfull[acc]);
+                    ++bit;
                 }
+                if (ok && step < n) {  // pass 1 of unit step -> accumulators A (0, 128)
+                    const uint32_t acc = ait & 1u;
+                    ok = tc::mbar_wait(&sm.aempty[acc], ((ait >> 1) & 1u) ^ 1u, abort, kLimitNs);
+                    tc::tc_fence_after();
+                    ok = ok && mma_chunk(step % kQSlots, tmem + acc * kChunk);
+                    if (ok) tc::mma_commit(&sm.afull[acc]);
+                    ++ait;
+                }
+            }
+            if (!ok) break;
+            // unit step-1 has had both passes: its Q slot is free once they finish
+            if (step > 0) tc::mma_commit(&sm.qempty[(step - 1) % kQSlots]);
+        }
+    } else if (warp >= 2 && warp < 2 + kGroupWarps) {
+        // ---------------- group A: pass 1 (row statistics) ----------------
+        const int ew = warp - 2;
+        const int quarter = warp & 3;  // TMEM lanes this warp may read
+        const int part = ew >> 2;      // which 64 columns of a chunk
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        uint32_t ait = 0;
+        for (int i = 0; i < n; ++i) {
+            float m = -INFINITY, l = 0.0f;
+            for (int c = 0; c < chunks; ++c, ++ait) {
+                const uint32_t acc = ait & 1u;
+                if (!tc::mbar_wait(&sm.afull[acc], (ait >> 1) & 1u, abort, kLimitNs)) goto a_done;
                 tc::tc_fence_after();
                 uint32_t r[2][32];
-                const uint32_t col = lane_addr + acc * kChunk + part * kPartCols;
+                const uint32_t col = lane_addr + acc * kChunk + part * 64;
                 tc::tmem_ld32(tmem + col, r[0]);
                 tc::tmem_ld32(tmem + col + 32, r[1]);
                 tc::tmem_ld_wait();
                 tc::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&sm.tempty[acc]);  // values are in registers now
+                warp_arrive(&sm.aempty[acc], lane);  // values are in registers now
                 float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(r[i >> 5][i & 31]));
+                for (int j = 0; j < 64; ++j) {
+                    mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(r[j >> 5][j & 31]));
                 }
                 const float gm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c2;
                 const float mn = fmaxf(m, gm);
                 float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    sum[i & 3] += ex2(fmaf(__uint_as_float(r[i >> 5][i & 31]), c2, -mn));
+                for (int j = 0; j < 64; ++j) {
+                    sum[j & 3] += ex2(fmaf(__uint_as_float(r[j >> 5][j & 31]), c2, -mn));
                 }
                 l = l * ex2(m - mn) + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
                 m = mn;
             }
-            // merge the four column parts of each row; the statistics travel in
-            // the staging tiles, once this warp's last TMA store has read them
-            __syncwarp();
-            reinterpret_cast<float2*>(tile)[lane] = make_float2(m, l);
-            named_sync(1, kEpiWarps * 32);
+            // hand (max, sum) of this part of the row to group B
             {
-                float2 st[kParts];
-#pragma unroll
-                for (int p = 0; p < kParts; ++p) {
-                    st[p] = reinterpret_cast<const float2*>(sm.out[4 * p + ((quarter + 2) & 3)])[lane];
+                const int slot = i & 1;
+                if (i >= 2 &&
+                    !tc::mbar_wait(&sm.sempty[slot], ((i >> 1) - 1) & 1, abort, kLimitNs)) {
+                    goto a_done;
                 }
-                float mm = st[0].x;
-#pragma unroll
-                for (int p = 1; p < kParts; ++p) mm = fmaxf(mm, st[p].x);
-                float ll = 0.0f;
-#pragma unroll
-                for (int p = 0; p < kParts; ++p) ll += st[p].y * ex2(st[p].x - mm);
-                m = mm;
-                l = ll;
+                sm.stats[slot][part][row] = make_float2(m, l);
+                warp_arrive(&sm.sfull[slot], lane);
             }
-            named_sync(1, kEpiWarps * 32);  // statistics read before the tiles are reused
-            const float inv = 1.0f / l;
-            // pass 2: recompute, normalise, transpose through the tile and store
-            for (int c = 0; c < chunks; ++c, ++acc_it) {
-                const uint32_t acc = acc_it & 1u;
-                if (!tc::mbar_wait(&sm.tfull[acc], (acc_it >> 1) & 1u, abort, kLimitNs)) {
-                    goto epi_done;
-                }
+        }
+    a_done:;
+    } else if (warp >= 2 + kGroupWarps) {
+        // ---------------- group B: pass 2 (normalised write) ----------------
+        const int ew = warp - 2 - kGroupWarps;
+        const int quarter = warp & 3;
+        const int part = ew >> 2;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        uint8_t* const tile = sm.out[ew];
+        const int jj = lane & 7;
+        uint32_t bit = 0;
+        for (int i = 0; i < n; ++i) {
+            const int u = unit_of(i);
+            const int b = u / bands, band = u - b * bands;
+            float m, inv;
+            {
+                const int slot = i & 1;
+                if (!tc::mbar_wait(&sm.sfull[slot], (i >> 1) & 1, abort, kLimitNs)) goto b_done;
+                const float2 s0 = sm.stats[slot][0][row], s1 = sm.stats[slot][1][row];
+                warp_arrive(&sm.sempty[slot], lane);
+                m = fmaxf(s0.x, s1.x);
+                const float l = s0.y * ex2(s0.x - m) + s1.y * ex2(s1.x - m);
+                // +inf score: the reference's exp(inf - inf) poisons the row
+                inv = (m == INFINITY) ? __int_as_float(0x7fffffff) : 1.0f / l;
+            }
+            float* const yband =
+                y + (static_cast<int64_t>(b) * s + band * kRows + quarter * 32) * s;
+            for (int c = 0; c < chunks; ++c, ++bit) {
+                const uint32_t acc = bit & 1u;
+                if (!tc::mbar_wait(&sm.bfull[acc], (bit >> 1) & 1u, abort, kLimitNs)) goto b_done;
                 tc::tc_fence_after();
-                const uint32_t col = lane_addr + acc * kChunk + part * kPartCols;
-                float* const ydst0 = y + static_cast<int64_t>(ybase_row) * s + c * kChunk +
-                                     part * kPartCols;
+                const uint32_t col = lane_addr + 256 + acc * kChunk + part * 64;
+                float* const ydst0 = yband + c * kChunk + part * 64;
 #pragma unroll 1
                 for (int g = 0; g < 2; ++g) {
                     uint32_t r[32];
@@ -271,8 +324,7 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                     tc::tmem_ld_wait();
                     if (g == 1) {
                         tc::tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) tc::mbar_arrive(&sm.tempty[acc]);
+                        warp_arrive(&sm.bempty[acc], lane);
                     }
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
@@ -287,13 +339,12 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                     __syncwarp();
                     // transpose through the tile: 8 lanes per row, 4 rows per
                     // instruction, every store a full 128-byte row segment
-                    const int jj = lane & 7;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int row = i * 4 + (lane >> 3);
+                    for (int t = 0; t < 8; ++t) {
+                        const int rr = t * 4 + (lane >> 3);
                         const float4 v = *reinterpret_cast<const float4*>(
-                            tile + row * 128 + ((jj ^ (row & 7)) << 4));
-                        __stcs(reinterpret_cast<float4*>(ydst0 + static_cast<int64_t>(row) * s +
+                            tile + rr * 128 + ((jj ^ (rr & 7)) << 4));
+                        __stcs(reinterpret_cast<float4*>(ydst0 + static_cast<int64_t>(rr) * s +
                                                          g * 32) + jj,
                                v);
                     }
@@ -301,8 +352,7 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                 }
             }
         }
-    epi_done:
-        __syncwarp();
+    b_done:;
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -362,14 +412,9 @@ extern "C" int mlkb_qk_softmax_f16(const void* q, const void* k, float* y, int64
     const int grid = static_cast<int>(units < smCount() ? units : smCount());
     // exp(scale * v) = exp2(scale * log2(e) * v)
     const float c2 = static_cast<float>(scale * 1.4426950408889634);
-    // About one pass (s/256 chunks of ~1.4 us each at d = 128) when each CTA
-    // has several units to amortise it.
-    const uint32_t stagger = units >= 4 * static_cast<int64_t>(grid)
-                                 ? static_cast<uint32_t>((s / kChunk) * 1400 * d / 128)
-                                 : 0u;
     qk_softmax_tcgen05<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, y, static_cast<int>(batch),
                                                           static_cast<int>(s), static_cast<int>(d),
-                                                          c2, stagger, deviceStatusPtr());
+                                                          c2, deviceStatusPtr());
     const cudaError_t le = cudaGetLastError();
     if (le != cudaSuccess) {
         cudaFuncAttributes fa{};

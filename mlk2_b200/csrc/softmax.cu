@@ -116,7 +116,8 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint3
 
 constexpr uint64_t kRowWaitLimitNs = 2000000000ull;
 
-// Row softmax, persistent CTAs: each CTA owns rows blockIdx.x + i*gridDim.x.
+// Row softmax, persistent CTAs (6 per SM at 4096 columns): each CTA owns rows
+// blockIdx.x + i*gridDim.x.
 // A TMA bulk copy brings row i+2 into a shared-memory double buffer while row
 // i is computed, so HBM reads stay in flight across the block reductions.
 // Thread t owns float4 vectors t + 256*j (j < NV) of its row; exponentials
@@ -336,7 +337,7 @@ int launchRowsTma(const float* x, float* y, int64_t rows, int64_t cols, cudaStre
         if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "softmax smem attribute");
         attr[dev] = true;
     }
-    const int per_sm = NV <= 2 ? 6 : NV <= 4 ? 4 : 2;
+    const int per_sm = NV <= 2 ? 8 : NV <= 4 ? 6 : 3;
     softmax_rows_tma<NV, kFull><<<rowGrid(rows, per_sm), kRowThreads, smem, s>>>(
         x, y, rows, cols, deviceStatusPtr());
     return checkLaunch("softmax launch");

@@ -397,21 +397,24 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
             d.update(extra)
         out[name] = d
 
-    # config 1: y = sin(x^2+3x), 2^24 f32 (64 MiB in: L2 flushed between steps)
-    n1 = 1 << 24
-    x = torch.empty(n1, device="cuda")
-    api.fill(x, SEED, 1 + 256 * rank, "uniform", -4.0, 4.0)
-    y = torch.empty_like(x)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    # config 1: y = sin(x^2+3x), 2^24 f32 (128 MiB touched per step). Steps
+    # rotate over 8 input/output pairs (1 GiB), so the pair a step uses was
+    # last touched 7 steps (896 MiB of traffic) earlier and is not in L2.
+    n1, nsets = 1 << 24, 8
+    xs1 = [torch.empty(n1, device="cuda") for _ in range(nsets)]
+    ys1 = [torch.empty_like(xs1[0]) for _ in range(nsets)]
+    for x in xs1:
+        api.fill(x, SEED, 1 + 256 * rank, "uniform", -4.0, 4.0)
+    turn = [0]
 
     def step1():
-        flush.zero_()
-        api.map_sin(x, y)
-    t_flush = time_device(torch, flush.zero_, warm, steps, dist, world)
-    sec = time_device(torch, step1, warm, steps, dist, world) - t_flush
+        i = turn[0] % nsets
+        turn[0] += 1
+        api.map_sin(xs1[i], ys1[i])
+    sec = time_device(torch, step1, warm, steps, dist, world)
     rec("map1", sec, n1 * 8, "GB/s", "hbm", peaks["hbm_gbs"], 1,
-        {"note": "L2 flushed by a 256 MiB memset before each step; its time subtracted"})
-    del x, y
+        {"note": "steps rotate over 8 input/output pairs (1 GiB > L2), no flush"})
+    del xs1, ys1
 
     # config 3: softmax [65536 x 4096] f32 per GPU
     xs = torch.empty((65536, 4096), device="cuda")

@@ -27,23 +27,21 @@ constexpr int kMapThreads = 256;
 constexpr int kMapUnroll = 2;  // float4 vectors per thread per step (plus a prefetched step)
 
 // Near-minimax polynomials on |r| <= pi/4 (fitted for this library by
-// weighted least squares on Chebyshev nodes): sin r = r + r^3 P(r^2) with
-// relative error < 6e-12, cos r = 1 + r^2 Q(r^2) with relative error < 7e-11
-// -- both far below f32 resolution (6e-8), which is all the f32-output
-// kernels need. cos(0) = 1 and sin(r) = r for tiny r hold exactly.
+// weighted least squares on Chebyshev nodes): sin r = r + r^3 S(r^2) with
+// relative error < 3.9e-9, cos r = 1 + r^2 C(r^2) with relative error
+// < 3.9e-8. An f32 result needs relative error below half an f32 ulp
+// (2^-25 = 3e-8 at worst, 6e-8 typically) for its rounding to land within one
+// ulp of the correctly rounded value; these stay there. cos(0) = 1 and
+// sin(r) = r for tiny r hold exactly.
 __device__ __forceinline__ double sin_r(double r, double z) {
-    double p = 2.717971090539634e-06;
-    p = fma(z, p, -0.00019839296518744639);
-    p = fma(z, p, 0.008333329256008314);
-    p = fma(z, p, -0.16666666640376984);
+    double p = fma(z, -0.0001951397821210659, 0.008332151315419242);
+    p = fma(z, p, -0.16666654462992936);
     return fma(r * z, p, r);
 }
 
 __device__ __forceinline__ double cos_r(double z) {
-    double p = 2.438187363435297e-05;
-    p = fma(z, p, -0.001388666363114334);
-    p = fma(z, p, 0.041666619786184696);
-    p = fma(z, p, -0.49999999689413566);
+    double p = fma(z, -0.0013590647071255219, 0.04165568770925181);
+    p = fma(z, p, -0.49999883312661797);
     return fma(z, p, 1.0);
 }
 
@@ -54,11 +52,18 @@ __device__ __forceinline__ double u_of(float x) {
     return fma(3.0, xd, xd * xd);
 }
 
-// |x| < 1000 keeps |u| < 2^20, the range of the two-term reduction.
+// |x| < 1000 for all four lanes keeps |u| < 2^20, the range of the two-term
+// reduction. A NaN lane is ignored by the max and takes the fast path, whose
+// arithmetic carries the NaN through to both outputs; inf fails the test.
 __device__ __forceinline__ bool fast_range(float4 v) {
-    const uint32_t a = __float_as_uint(v.x) & 0x7fffffffu, b = __float_as_uint(v.y) & 0x7fffffffu;
-    const uint32_t c = __float_as_uint(v.z) & 0x7fffffffu, d = __float_as_uint(v.w) & 0x7fffffffu;
-    return max(max(a, b), max(c, d)) < 0x447a0000u;  // 1000.0f
+    const float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    return m < 1000.0f;
+}
+
+// Sign bit 31 set when bit 1 of q is: the quadrant's sign flip, applied to the
+// rounded f32 (round-to-nearest is symmetric, so this equals rounding -v).
+__device__ __forceinline__ float flip_if(float v, int q) {
+    return __uint_as_float(__float_as_uint(v) ^ ((static_cast<uint32_t>(q) << 30) & 0x80000000u));
 }
 
 struct SinOp {
@@ -68,7 +73,7 @@ struct SinOp {
         const double r = dev::reduce_pio2(u_of(x), q);
         const double z = r * r;
         const double v = (q & 1) ? cos_r(z) : sin_r(r, z);
-        y0 = static_cast<float>((q & 2) ? -v : v);
+        y0 = flip_if(static_cast<float>(v), q);
     }
     __device__ __noinline__ static float2 slow(float x) {
         return make_float2(static_cast<float>(dev::sin_f64(u_of(x))), 0.0f);
@@ -83,13 +88,12 @@ struct SinDsinOp {
         const double z = r * r;
         const double sr = sin_r(r, z), cr = cos_r(z);
         // quadrant q: (sin u, cos u) = (sr, cr), (cr, -sr), (-sr, -cr), (-cr, sr)
-        double a = (q & 1) ? cr : sr;
-        double b = (q & 1) ? sr : cr;
-        a = (q & 2) ? -a : a;
-        const double g = fma(2.0, static_cast<double>(x), 3.0);  // 2x + 3, exact
-        const double gs = ((q + 1) & 2) ? -g : g;
-        y0 = static_cast<float>(a);
-        y1 = static_cast<float>(b * gs);
+        const bool odd = (q & 1) != 0;
+        const double a = odd ? cr : sr;
+        const double b = odd ? sr : cr;
+        const double g = fma(2.0, static_cast<double>(x), 3.0);  // fl64(2x + 3), as the reference
+        y0 = flip_if(static_cast<float>(a), q);
+        y1 = flip_if(static_cast<float>(b * g), q + 1);
     }
     __device__ __noinline__ static float2 slow(float x) {
         double s, c;

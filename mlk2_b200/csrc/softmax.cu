@@ -20,6 +20,7 @@ namespace {
 
 constexpr int kRowThreads = 256;
 constexpr int kRowWarps = kRowThreads / 32;
+static_assert(kRowThreads == 256, "the exp table is filled one entry per thread");
 
 __device__ __forceinline__ float warpMax(float v) {
 #pragma unroll
@@ -36,19 +37,7 @@ __device__ __forceinline__ double warpSum(double v) {
     return v;
 }
 
-// Block-wide max / sum over kRowThreads threads; every thread gets the result.
-__device__ __forceinline__ float blockMax(float v, float* sm) {
-    v = warpMax(v);
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    if (l == 0) sm[w] = v;
-    __syncthreads();
-    float r = sm[0];
-#pragma unroll
-    for (int i = 1; i < kRowWarps; ++i) r = (sm[i] > r) ? sm[i] : r;
-    __syncthreads();
-    return r;
-}
-
+// Block-wide sum over kRowThreads threads; every thread gets the result.
 __device__ __forceinline__ double blockSum(double v, double* sm) {
     v = warpSum(v);
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -61,46 +50,25 @@ __device__ __forceinline__ double blockSum(double v, double* sm) {
     return r;
 }
 
-// 2^(j/64), j = 0..63, correctly rounded f64.
-__device__ const double kExp2Tab[64] = {
-    1.0, 1.0108892860517005, 1.0218971486541166, 1.0330248790212284,
-    1.0442737824274138, 1.0556451783605572, 1.0671404006768237, 1.0787607977571199,
-    1.0905077326652577, 1.102382583307841, 1.1143867425958924, 1.1265216186082418,
-    1.1387886347566916, 1.1511892299529827, 1.1637248587775775, 1.1763969916502812,
-    1.189207115002721, 1.202156731452703, 1.215247359980469, 1.22848053610687,
-    1.241857812073484, 1.255380757024691, 1.2690509571917332, 1.2828700160787783,
-    1.2968395546510096, 1.3109612115247644, 1.3252366431597413, 1.339667524053303,
-    1.3542555469368927, 1.3690024229745905, 1.383909881963832, 1.3989796725383112,
-    1.4142135623730951, 1.42961333839197, 1.4451808069770467, 1.460917794180647,
-    1.4768261459394993, 1.4929077282912648, 1.5091644275934228, 1.5255981507445384,
-    1.5422108254079407, 1.559004400237837, 1.5759808451078865, 1.593142151342267,
-    1.6104903319492543, 1.6280274218573478, 1.645755478153965, 1.6636765803267364,
-    1.681792830507429, 1.7001063537185235, 1.718619298122478, 1.7373338352737062,
-    1.7562521603732995, 1.7753764925265212, 1.7947090750031072, 1.8142521755003989,
-    1.8340080864093424, 1.8539791250833855, 1.8741676341103, 1.8945759815869656,
-    1.9152065613971474, 1.9360617934922943, 1.9571441241754002, 1.978456026387951,
-};
-
-// exp(d) in f64 for d <= 0: k = rint(64 d / ln2), r = d - k ln2/64 (two-term
-// constant; the first product is exact under FMA), |r| <= ln2/128, so a cubic
-// in r has relative error < 4e-11; then 2^(k/64) = 2^(k>>6) * T[k&63] with the
-// power of two added to T's exponent field. d < -120 gives 0 (such terms are
-// below half the smallest f32 subnormal relative to any row sum >= 1 and add
-// nothing to it); NaN propagates; -inf gives 0.
+// exp(d) in f64 for d <= 0: k = rint(256 d / ln2), r = d - k ln2/256 (one
+// FMA with fl64(ln2/256): |k| <= 44320 keeps the constant's error below 1e-14
+// relative), |r| <= ln2/512, so 1 + r + r^2/2 has relative error < 4.2e-10
+// (under 0.01 f32 ulp); then 2^(k/256) = 2^(k>>8) * T[k&255] with the power
+// of two added to T's exponent field. d < -120 gives 0 (such terms are below
+// half the smallest f32 subnormal relative to any row sum >= 1 and add
+// nothing to it); NaN propagates; -inf gives 0. tab[j] = 2^(j/256).
 __device__ __forceinline__ double exp_neg_tab(double d, const double* tab) {
-    // Branch-free: every lane evaluates the formula (the table index k & 63 is
+    // Branch-free: every lane evaluates the formula (the table index k & 255 is
     // always in range), then out-of-range lanes take 0 or their NaN.
-    const double kMagic = 6755399441055744.0;
-    const double t = fma(d, 92.33248261689366, kMagic);
+    const double kMagic = 6755399441055744.0;  // 1.5 * 2^52
+    const double t = fma(d, 369.3299304675746, kMagic);
     const double kd = t - kMagic;
     const int k = __double2loint(t);
-    double r = fma(-kd, 0.010830424696249145, d);
-    r = fma(-kd, 3.623510646634843e-19, r);
-    double p = fma(r, 0.16666666666666666, 0.5);
+    const double r = fma(-kd, 0.0027076061740622863, d);
+    double p = fma(r, 0.5, 1.0);
     p = fma(p, r, 1.0);
-    p = fma(p, r, 1.0);
-    const double tj = tab[k & 63];
-    const double scale = __hiloint2double(__double2hiint(tj) + ((k >> 6) << 20),
+    const double tj = tab[k & 255];
+    const double scale = __hiloint2double(__double2hiint(tj) + ((k >> 8) << 20),
                                           __double2loint(tj));
     const double e = p * scale;
     return (d >= -120.0) ? e : ((d != d) ? d : 0.0);
@@ -120,6 +88,8 @@ constexpr uint64_t kRowWaitLimitNs = 2000000000ull;
 // blockIdx.x + i*gridDim.x.
 // A TMA bulk copy brings row i+2 into a shared-memory double buffer while row
 // i is computed, so HBM reads stay in flight across the block reductions.
+// Two block barriers per row: one for the max (it also carries the vote on
+// the bounded wait), one for the sum.
 // Thread t owns float4 vectors t + 256*j (j < NV) of its row; exponentials
 // are kept in registers between the sum and the write (read once, write
 // once). cols % 4 == 0, cols <= 1024*NV, 16-byte aligned rows.
@@ -129,7 +99,7 @@ softmax_rows_tma(const float* __restrict__ x, float* __restrict__ y, int64_t row
                  int64_t cols, int* __restrict__ status) {
     extern __shared__ __align__(128) uint8_t dyn[];
     __shared__ uint64_t full[2];
-    __shared__ double tab[64];
+    __shared__ double tab[256];
     __shared__ float smax[kRowWarps];
     __shared__ double ssum[kRowWarps];
     const uint32_t row_bytes = static_cast<uint32_t>(cols) * 4u;
@@ -141,7 +111,7 @@ softmax_rows_tma(const float* __restrict__ x, float* __restrict__ y, int64_t row
         tc::mbar_init(&full[1], 1);
         tc::fence_barrier_init();
     }
-    if (tid < 64) tab[tid] = kExp2Tab[tid];
+    tab[tid] = exp2(static_cast<double>(tid) * (1.0 / 256.0));  // kRowThreads == 256
     __syncthreads();
     if (tid == 0) {
         for (int b = 0; b < 2; ++b) {
@@ -152,15 +122,12 @@ softmax_rows_tma(const float* __restrict__ x, float* __restrict__ y, int64_t row
             }
         }
     }
+    const int warp = tid >> 5, lane = tid & 31;
     int it = 0;
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
         const int b = it & 1;
         int never = 0;
         const bool ok = tc::mbar_wait(&full[b], (it >> 1) & 1, &never, kRowWaitLimitNs);
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0 && status != nullptr) atomicExch(status, MLKB_ERR_TIMEOUT);
-            break;
-        }
         const float4* xr = reinterpret_cast<const float4*>(dyn + b * buf_bytes);
         float4 v[NV];
         float m = -INFINITY;
@@ -175,7 +142,20 @@ softmax_rows_tma(const float* __restrict__ x, float* __restrict__ y, int64_t row
                 m = (v[j].w > m) ? v[j].w : m;
             }
         }
-        m = blockMax(m, smax);  // every thread has read buffer b past this barrier
+        m = warpMax(m);
+        if (lane == 0) smax[warp] = m;
+        // Barrier A (one of two per row): publishes the warp maxima, votes on
+        // the wait outcome, and marks buffer b as read by every thread. The
+        // previous row's sums were read before any thread got here, and this
+        // row's maxima are read before barrier B, so one slot array each is
+        // enough.
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0 && status != nullptr) atomicExch(status, MLKB_ERR_TIMEOUT);
+            break;
+        }
+        m = smax[0];
+#pragma unroll
+        for (int i = 1; i < kRowWarps; ++i) m = (smax[i] > m) ? smax[i] : m;
         if (tid == 0) {
             const int64_t nxt = row + 2 * static_cast<int64_t>(gridDim.x);
             if (nxt < rows) {
@@ -198,19 +178,24 @@ softmax_rows_tma(const float* __restrict__ x, float* __restrict__ y, int64_t row
                 s += (e[j][0] + e[j][1]) + (e[j][2] + e[j][3]);
             }
         }
-        s = blockSum(s, ssum);
-        const bool nz = (s != 0.0);
-        const double inv = nz ? 1.0 / s : 0.0;
+        s = warpSum(s);
+        if (lane == 0) ssum[warp] = s;
+        __syncthreads();  // barrier B: the warp sums
+        s = 0.0;
+#pragma unroll
+        for (int i = 0; i < kRowWarps; ++i) s += ssum[i];
+        // s == 0 only if every e is 0, so e * 0 gives the reference's 0.
+        const double inv = (s != 0.0) ? 1.0 / s : 0.0;
         float4* yr = reinterpret_cast<float4*>(y + row * cols);
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
             const int c = tid + j * kRowThreads;
             if (kFull || c < nvec) {
                 float4 o;
-                o.x = nz ? static_cast<float>(e[j][0] * inv) : 0.0f;
-                o.y = nz ? static_cast<float>(e[j][1] * inv) : 0.0f;
-                o.z = nz ? static_cast<float>(e[j][2] * inv) : 0.0f;
-                o.w = nz ? static_cast<float>(e[j][3] * inv) : 0.0f;
+                o.x = static_cast<float>(e[j][0] * inv);
+                o.y = static_cast<float>(e[j][1] * inv);
+                o.z = static_cast<float>(e[j][2] * inv);
+                o.w = static_cast<float>(e[j][3] * inv);
                 __stcs(yr + c, o);
             }
         }

@@ -2,7 +2,11 @@
 // TMEM, f32 output, all row-major (reference gemmRowBlock,
 // runtime/src/execution/kernel_buffers.cpp:406-432, which accumulates into C).
 //
-// Blackwell design (one CTA per SM, persistent over 128x256 output tiles):
+// Plain GEMMs ([K,N] B, no batch) run on CTA pairs (gemm_f16_tcgen05_pair,
+// 256x256 tiles, tcgen05 cta_group::2); the batched / K-major-B form used by
+// the scaled-scores fallback runs on single CTAs.
+//
+// Single-CTA design (one CTA per SM, persistent over 128x256 output tiles):
 //   warp 0      TMA producer: A tile [128 x 64] (K-major, 128B swizzle) and
 //               B tile [64 x 256] as four [64 x 64] boxes (N-major, 128B
 //               swizzle) per stage into a 4-stage shared-memory ring;
@@ -225,6 +229,181 @@ gemm_f16_tcgen05(const __grid_constant__ CUtensorMap tma_a,
     if (threadIdx.x == 0 && s.abort && status != nullptr) atomicExch(status, MLKB_ERR_TIMEOUT);
 }
 
+// ---- CTA-pair variant: 256 x 256 tiles over a cluster of two SMs ------------
+// tcgen05.mma.cta_group::2 M256 N256 K16: the even CTA of the pair issues the
+// MMAs; each CTA stages its own 128 rows of A and its own 128 columns of B
+// (half the B traffic of the one-CTA kernel per output element, and each SM's
+// tensor core reads 8 KB of shared memory per K16 step instead of 12 KB).
+// Both CTAs' TMA loads complete on the even CTA's `full` barrier; the MMA
+// commit multicasts stage release and accumulator-ready to both CTAs; both
+// epilogues report a drained accumulator on the even CTA's `tempty`.
+constexpr int kPairStages = 6;
+constexpr uint32_t kBHalf = kBK * (kBN / 2) * 2;  // 16 KB: [64 K-rows x 128 N]
+
+struct PairSmem {
+    uint8_t a[kPairStages][kAStage];
+    uint8_t b[kPairStages][kBHalf];
+    uint64_t full[kPairStages];
+    uint64_t empty[kPairStages];
+    uint64_t tfull[2];
+    uint64_t tempty[2];
+    uint32_t tmem_base;
+    int abort;
+};
+
+constexpr size_t kPairSmemBytes = sizeof(PairSmem) + 1024;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm_f16_tcgen05_pair(const __grid_constant__ CUtensorMap tma_a,
+                      const __grid_constant__ CUtensorMap tma_b, float* __restrict__ c, int m,
+                      int n, int k, int accumulate, int* __restrict__ status) {
+    extern __shared__ uint8_t smem_raw[];
+    PairSmem& s = *reinterpret_cast<PairSmem*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = tc::cluster_ctarank();
+    const bool leader = (rank == 0);
+    const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+    const int mt = (m + 2 * kBM - 1) / (2 * kBM), nt = (n + kBN - 1) / kBN;
+    const int kt = (k + kBK - 1) / kBK;
+    const int tiles = mt * nt;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kPairStages; ++i) {
+            tc::mbar_init(&s.full[i], 1);
+            tc::mbar_init(&s.empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&s.tfull[i], 1);
+            tc::mbar_init(&s.tempty[i], 2 * 4);  // the epilogue warps of both CTAs
+        }
+        s.abort = 0;
+        tc::fence_barrier_init();
+        tc::fence_proxy_async();
+    }
+    if (warp == 0) tc::tmem_alloc_pair(&s.tmem_base, 512);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::cluster_sync();  // barriers of both CTAs initialised before any remote use
+    tc::tc_fence_after();
+    const uint32_t tmem = s.tmem_base;
+    volatile int* abort = &s.abort;
+
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer (both CTAs): own A rows and own half of B ----
+        tc::prefetch_tmap(&tma_a);
+        tc::prefetch_tmap(&tma_b);
+        uint32_t it = 0;
+        for (int tile = pair; tile < tiles && !*abort; tile += pairs) {
+            int mb, nb;
+            tileCoords(tile, mt, nt, mb, nb);
+            const int arow = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+            const int bcol = nb * kBN + static_cast<int>(rank) * (kBN / 2);
+            for (int kb = 0; kb < kt; ++kb, ++it) {
+                const int st = static_cast<int>(it % kPairStages);
+                const uint32_t ph = (it / kPairStages) & 1u;
+                if (!tc::mbar_wait(&s.empty[st], ph ^ 1u, abort, kWaitLimitNs)) goto producer_done;
+                if (leader) tc::mbar_arrive_expect_tx(&s.full[st], 2 * (kAStage + kBHalf));
+                const uint32_t bar = tc::mapa_shared(tc::smem_u32(&s.full[st]), 0);
+                tc::tma_load_2d_pair(s.a[st], &tma_a, bar, kb * kBK, arow);
+                tc::tma_load_2d_pair(s.b[st], &tma_b, bar, bcol, kb * kBK);
+                tc::tma_load_2d_pair(s.b[st] + kBBox, &tma_b, bar, bcol + 64, kb * kBK);
+            }
+        }
+    producer_done:
+        // The even CTA's full barriers count both CTAs' bytes: draining them
+        // there covers every load of the pair (the final cluster barrier keeps
+        // the odd CTA alive until then).
+        if (leader) {
+            for (uint32_t j = it > kPairStages ? it - kPairStages : 0; j < it; ++j) {
+                drainWait(&s.full[j % kPairStages], (j / kPairStages) & 1u);
+            }
+        }
+    } else if (warp == 1 && lane == 0 && leader) {
+        // ---- MMA issuer (even CTA only) ----
+        constexpr uint32_t kIdesc = tc::idesc_f16_f32(2 * kBM, kBN, 0, 1);
+        uint32_t it = 0, local = 0;
+        for (int tile = pair; tile < tiles; tile += pairs, ++local) {
+            const uint32_t acc = local & 1u, aph = (local >> 1) & 1u;
+            if (!tc::mbar_wait(&s.tempty[acc], aph ^ 1u, abort, kWaitLimitNs)) break;
+            tc::tc_fence_after();
+            const uint32_t d = tmem + acc * kBN;
+            for (int kb = 0; kb < kt; ++kb, ++it) {
+                const int st = static_cast<int>(it % kPairStages);
+                const uint32_t ph = (it / kPairStages) & 1u;
+                if (!tc::mbar_wait(&s.full[st], ph, abort, kWaitLimitNs)) goto mma_done;
+                tc::tc_fence_after();
+                const uint32_t a0 = tc::smem_u32(s.a[st]);
+                const uint32_t b0 = tc::smem_u32(s.b[st]);
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                    const uint64_t ad = tc::smem_desc_sw128(a0 + kk * 32, 16, 1024);
+                    const uint64_t bd = tc::smem_desc_sw128(b0 + kk * 2048, kBBox, 1024);
+                    tc::mma_f16_pair(d, ad, bd, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc::mma_commit_pair(&s.empty[st], 0x3);
+            }
+            tc::mma_commit_pair(&s.tfull[acc], 0x3);
+        }
+    mma_done:;
+    } else if (warp >= 2) {
+        // ---- epilogue (both CTAs): own 128 rows x 256 columns ----
+        const int quarter = warp & 3;
+        const int row_in_tile = static_cast<int>(rank) * kBM + quarter * 32 + lane;
+        uint32_t local = 0;
+        for (int tile = pair; tile < tiles; tile += pairs, ++local) {
+            int mb, nb;
+            tileCoords(tile, mt, nt, mb, nb);
+            const uint32_t acc = local & 1u, aph = (local >> 1) & 1u;
+            if (!tc::mbar_wait(&s.tfull[acc], aph, abort, kWaitLimitNs)) break;
+            tc::tc_fence_after();
+            const int64_t row = static_cast<int64_t>(mb) * 2 * kBM + row_in_tile;
+            float* crow = c + row * n;
+#pragma unroll 1
+            for (int cc = 0; cc < kBN / 32; ++cc) {
+                uint32_t r[32];
+                tc::tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN +
+                                  cc * 32,
+                              r);
+                tc::tmem_ld_wait();
+                const int col0 = nb * kBN + cc * 32;
+                if (row < m) {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const int col = col0 + q * 4;
+                        if (col < n) {
+                            float4 v = make_float4(__uint_as_float(r[4 * q]),
+                                                   __uint_as_float(r[4 * q + 1]),
+                                                   __uint_as_float(r[4 * q + 2]),
+                                                   __uint_as_float(r[4 * q + 3]));
+                            float4* dst = reinterpret_cast<float4*>(crow + col);
+                            if (accumulate) {
+                                const float4 o = *dst;
+                                v.x += o.x;
+                                v.y += o.y;
+                                v.z += o.z;
+                                v.w += o.w;
+                            }
+                            *dst = v;
+                        }
+                    }
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive_cluster(tc::mapa_shared(tc::smem_u32(&s.tempty[acc]), 0));
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::cluster_sync();  // no MMA, load or remote arrive of the pair is still pending
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc_pair(tmem, 512);
+    }
+    if (threadIdx.x == 0 && s.abort && status != nullptr) atomicExch(status, MLKB_ERR_TIMEOUT);
+}
+
 // Generic SIMT fallback for shapes or alignments TMA cannot take
 // (K or N not a multiple of 8, or unaligned bases).
 __global__ void gemm_f16_simt(const __half* __restrict__ a, const __half* __restrict__ b,
@@ -316,6 +495,33 @@ int launchGemmTc(const void* a, const void* b, float* c, int64_t batch, int64_t 
     return checkLaunch("gemm tcgen05 launch");
 }
 
+// Launches the CTA-pair tcgen05 GEMM (B is [k, n] row-major, no batch, no
+// scale). Returns MLKB_ERR_LAUNCH when a pair launch is refused, so the caller
+// can take the one-CTA kernel.
+int launchGemmPair(const void* a, const void* b, float* c, int64_t m, int64_t n, int64_t k,
+                   int accumulate, cudaStream_t s) {
+    CUtensorMap ta, tb;
+    if (int st = makeTmapF16(&ta, a, m, k, kBM, kBK)) return st;
+    if (int st = makeTmapF16(&tb, b, k, n, kBK, 64)) return st;
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(gemm_f16_tcgen05_pair,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kPairSmemBytes));
+        if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "gemm pair smem attribute");
+        attr[dev] = true;
+    }
+    const int64_t tiles = ((m + 2 * kBM - 1) / (2 * kBM)) * ((n + kBN - 1) / kBN);
+    const int64_t pairs_max = smCount() / 2;
+    const int grid = 2 * static_cast<int>(tiles < pairs_max ? tiles : pairs_max);
+    gemm_f16_tcgen05_pair<<<grid, kThreads, kPairSmemBytes, s>>>(
+        ta, tb, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), accumulate,
+        deviceStatusPtr());
+    return checkLaunch("gemm tcgen05 pair launch");
+}
+
 }  // namespace mlkb
 
 extern "C" int mlkb_gemm_f16_f32(const void* a, const void* b, float* c, int64_t m, int64_t n,
@@ -335,6 +541,9 @@ extern "C" int mlkb_gemm_f16_f32(const void* a, const void* b, float* c, int64_t
                                            static_cast<const __half*>(b), c, m, n, k,
                                            accumulate ? 1 : 0);
         return checkLaunch("gemm f16 simt launch");
+    }
+    if (smCount() >= 2 && launchGemmPair(a, b, c, m, n, k, accumulate ? 1 : 0, s) == MLKB_OK) {
+        return MLKB_OK;
     }
     return launchGemmTc(a, b, c, 1, m, n, k, false, accumulate ? 1 : 0, 1.0f, s);
 }

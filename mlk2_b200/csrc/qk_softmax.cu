@@ -75,6 +75,13 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// max of three (NaN-avoiding like fmaxf: a NaN operand never wins).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // Lane-0 arrive after the whole warp is done with the guarded resource.
 __device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
     __syncwarp();
@@ -260,17 +267,23 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                 warp_arrive(&sm.aempty[acc], lane);  // values are in registers now
                 float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int j = 0; j < 64; ++j) {
-                    mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(r[j >> 5][j & 31]));
+                for (int j = 0; j < 64; j += 2) {
+                    mx[(j >> 1) & 3] = max3(mx[(j >> 1) & 3], __uint_as_float(r[j >> 5][j & 31]),
+                                            __uint_as_float(r[j >> 5][(j & 31) + 1]));
                 }
-                const float gm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c2;
+                const float gm = max3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * c2;
                 const float mn = fmaxf(m, gm);
-                float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                // exponent arguments and partial sums two at a time (packed f32x2)
+                float2 sum[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
 #pragma unroll
-                for (int j = 0; j < 64; ++j) {
-                    sum[j & 3] += ex2(fmaf(__uint_as_float(r[j >> 5][j & 31]), c2, -mn));
+                for (int j = 0; j < 64; j += 2) {
+                    const float2 t = __ffma2_rn(make_float2(__uint_as_float(r[j >> 5][j & 31]),
+                                                            __uint_as_float(r[j >> 5][(j & 31) + 1])),
+                                                make_float2(c2, c2), make_float2(-mn, -mn));
+                    sum[(j >> 1) & 1] =
+                        __fadd2_rn(sum[(j >> 1) & 1], make_float2(ex2(t.x), ex2(t.y)));
                 }
-                l = l * ex2(m - mn) + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
+                l = l * ex2(m - mn) + ((sum[0].x + sum[0].y) + (sum[1].x + sum[1].y));
                 m = mn;
             }
             // hand (max, sum) of this part of the row to group B
@@ -298,16 +311,16 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
         for (int i = 0; i < n; ++i) {
             const int u = unit_of(i);
             const int b = u / bands, band = u - b * bands;
-            float m, inv;
+            float mi;  // m + log2(l): y = exp2(s * c2 - mi) = exp2(s * c2 - m) / l
             {
                 const int slot = i & 1;
                 if (!tc::mbar_wait(&sm.sfull[slot], (i >> 1) & 1, abort, kLimitNs)) goto b_done;
                 const float2 s0 = sm.stats[slot][0][row], s1 = sm.stats[slot][1][row];
                 warp_arrive(&sm.sempty[slot], lane);
-                m = fmaxf(s0.x, s1.x);
+                const float m = fmaxf(s0.x, s1.x);
                 const float l = s0.y * ex2(s0.x - m) + s1.y * ex2(s1.x - m);
                 // +inf score: the reference's exp(inf - inf) poisons the row
-                inv = (m == INFINITY) ? __int_as_float(0x7fffffff) : 1.0f / l;
+                mi = (m == INFINITY) ? __int_as_float(0x7fffffff) : m + log2f(l);
             }
             float* const yband =
                 y + (static_cast<int64_t>(b) * s + band * kRows + quarter * 32) * s;
@@ -328,11 +341,18 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                     }
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
+                        // exponent arguments two at a time (packed f32x2 FMA)
+                        const float2 t0 = __ffma2_rn(
+                            make_float2(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1])),
+                            make_float2(c2, c2), make_float2(-mi, -mi));
+                        const float2 t1 = __ffma2_rn(
+                            make_float2(__uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])),
+                            make_float2(c2, c2), make_float2(-mi, -mi));
                         float4 v;
-                        v.x = ex2(fmaf(__uint_as_float(r[4 * j + 0]), c2, -m)) * inv;
-                        v.y = ex2(fmaf(__uint_as_float(r[4 * j + 1]), c2, -m)) * inv;
-                        v.z = ex2(fmaf(__uint_as_float(r[4 * j + 2]), c2, -m)) * inv;
-                        v.w = ex2(fmaf(__uint_as_float(r[4 * j + 3]), c2, -m)) * inv;
+                        v.x = ex2(t0.x);
+                        v.y = ex2(t0.y);
+                        v.z = ex2(t1.x);
+                        v.w = ex2(t1.y);
                         // row `lane`, 16-byte chunk j, XOR-swizzled (conflict-free)
                         *reinterpret_cast<float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4)) = v;
                     }

@@ -39,7 +39,8 @@ constexpr uint32_t kBBox = kBK * 64 * 2;     // 8 KB: [64 K-rows x 64 N]
 constexpr uint32_t kBStage = kBK * kBN * 2;  // 32 KB
 constexpr int kThreads = 192;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
-constexpr int kGroupM = 16;
+constexpr int kGroupM = 16;     // one-CTA kernel: 16 x 128-row M-blocks
+constexpr int kPairGroupM = 8;  // pair kernel: 8 x 256-row M-blocks
 
 struct GemmSmem {
     uint8_t a[kStages][kAStage];
@@ -54,11 +55,14 @@ struct GemmSmem {
 
 constexpr size_t kSmemBytes = sizeof(GemmSmem) + 1024;
 
+// Tiles are visited in groups of G M-blocks (all N-blocks of a group before
+// the next group) so the A and B panels in flight stay L2-resident.
+template <int G>
 __device__ __forceinline__ void tileCoords(int tile, int mt, int nt, int& mb, int& nb) {
-    const int per_group = kGroupM * nt;
+    const int per_group = G * nt;
     const int g = tile / per_group;
-    const int first = g * kGroupM;
-    const int gsize = (mt - first) < kGroupM ? (mt - first) : kGroupM;
+    const int first = g * G;
+    const int gsize = (mt - first) < G ? (mt - first) : G;
     const int r = tile % per_group;
     mb = first + r % gsize;
     nb = r / gsize;
@@ -115,7 +119,7 @@ gemm_f16_tcgen05(const __grid_constant__ CUtensorMap tma_a,
         for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
             const int bt = tile / per_batch;
             int mb, nb;
-            tileCoords(tile - bt * per_batch, mt, nt, mb, nb);
+            tileCoords<kGroupM>(tile - bt * per_batch, mt, nt, mb, nb);
             const int arow = bt * m + mb * kBM;
             for (int kb = 0; kb < kt; ++kb) {
                 const int st = static_cast<int>(it % kStages);
@@ -180,7 +184,7 @@ gemm_f16_tcgen05(const __grid_constant__ CUtensorMap tma_a,
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             const int bt = tile / per_batch;
             int mb, nb;
-            tileCoords(tile - bt * per_batch, mt, nt, mb, nb);
+            tileCoords<kGroupM>(tile - bt * per_batch, mt, nt, mb, nb);
             const uint32_t acc = local & 1u, aph = (local >> 1) & 1u;
             if (!tc::mbar_wait(&s.tfull[acc], aph, abort, kWaitLimitNs)) break;
             tc::tc_fence_after();
@@ -296,7 +300,7 @@ gemm_f16_tcgen05_pair(const __grid_constant__ CUtensorMap tma_a,
         uint32_t it = 0;
         for (int tile = pair; tile < tiles && !*abort; tile += pairs) {
             int mb, nb;
-            tileCoords(tile, mt, nt, mb, nb);
+            tileCoords<kPairGroupM>(tile, mt, nt, mb, nb);
             const int arow = mb * 2 * kBM + static_cast<int>(rank) * kBM;
             const int bcol = nb * kBN + static_cast<int>(rank) * (kBN / 2);
             for (int kb = 0; kb < kt; ++kb, ++it) {
@@ -353,7 +357,7 @@ gemm_f16_tcgen05_pair(const __grid_constant__ CUtensorMap tma_a,
         uint32_t local = 0;
         for (int tile = pair; tile < tiles; tile += pairs, ++local) {
             int mb, nb;
-            tileCoords(tile, mt, nt, mb, nb);
+            tileCoords<kPairGroupM>(tile, mt, nt, mb, nb);
             const uint32_t acc = local & 1u, aph = (local >> 1) & 1u;
             if (!tc::mbar_wait(&s.tfull[acc], aph, abort, kWaitLimitNs)) break;
             tc::tc_fence_after();

@@ -11,18 +11,22 @@
 // roofline, so every score is written exactly once and nothing else is. Each
 // unit needs two passes over its scores (row statistics, then the normalised
 // write); running them back to back would leave HBM idle during the first.
-// Instead the CTA overlaps pass 1 of unit i with pass 2 of unit i-1:
+// Instead the CTA overlaps pass 1 of unit i with pass 2 of unit i-1. Each CTA
+// takes runs of consecutive bands of one batch, so units i-1 and i mostly
+// share a batch and then one K load feeds both passes' MMAs.
 //   warp 0       TMA producer: Q bands into three slots, K in [128 x 64] boxes
 //                through a 5-stage ring, in the MMA's consumption order;
 //   warp 1       MMA issuer: per 128-column chunk, tcgen05.mma M128 N128 K16
 //                (both operands K-major) for pass 2 of unit i-1 and pass 1 of
 //                unit i, into four 128-column TMEM accumulators (two per pass);
-//   warps 2-9    group A (pass 1), two warps per TMEM lane quarter: online row
+//   warps 2-5    group A (pass 1), one warp per TMEM lane quarter: online row
 //                max / sum of exp2(scale*log2e*s), handed to group B through a
 //                double-buffered statistics slot;
-//   warps 10-17  group B (pass 2): recompute, normalise, transpose through an
-//                XOR-swizzled shared-memory tile so every global store is a
-//                full 128-byte row segment.
+//   warps 6-13   group B (pass 2), two warps per lane quarter: recompute,
+//                exp2(s*c - (m + log2 l)), transpose through an XOR-swizzled
+//                shared-memory tile so every global store is a full 128-byte
+//                row segment; the TMEM load of a warp's second 32-column group
+//                is in flight while its first is written.
 // Every mbarrier wait is bounded (2 s); on a timeout the CTA raises the
 // device status word, drains its copies, frees TMEM and returns.
 // Other shapes use the two-step form (tcgen05 GEMM with the scale folded into
@@ -46,19 +50,21 @@ namespace {
 constexpr int kRows = 128;   // score rows per unit (M of the MMA)
 constexpr int kChunk = 128;  // score columns per accumulator (N of the MMA)
 constexpr int kKStages = 5;  // K ring depth, [128 x 64] f16 boxes
+constexpr int kRun = 4;      // consecutive bands of one batch per CTA
 constexpr int kQSlots = 3;   // Q bands resident: units i-1, i and the prefetched i+1
 constexpr uint32_t kKBox = kChunk * 64 * 2;  // 16 KB
 constexpr uint32_t kQBox = kRows * 64 * 2;   // 16 KB (one d-half)
-constexpr int kGroupWarps = 8;               // per epilogue group, 2 per lane quarter
-constexpr int kThreads = 64 + 2 * kGroupWarps * 32;  // 576
+constexpr int kAWarps = 4;                   // pass 1: one warp per lane quarter
+constexpr int kBWarps = 8;                   // pass 2: two warps per lane quarter
+constexpr int kThreads = 64 + (kAWarps + kBWarps) * 32;  // 448
 constexpr uint32_t kStageTile = 32 * 32 * 4;         // [32 rows x 32 cols] f32
 constexpr uint64_t kLimitNs = 2000000000ull;
 
 struct QkSmem {
     uint8_t k[kKStages][kKBox];              // 80 KB
     uint8_t q[kQSlots][2][kQBox];            // 96 KB
-    uint8_t out[kGroupWarps][kStageTile];    // 32 KB (group B staging)
-    float2 stats[2][2][kRows];               // [slot][part][row] = (max, sum)
+    uint8_t out[kBWarps][kStageTile];        // 32 KB (group B staging)
+    float2 stats[2][kRows];                  // [slot][row] = (max, sum)
     uint64_t kfull[kKStages], kempty[kKStages];
     uint64_t qfull[kQSlots], qempty[kQSlots];
     uint64_t afull[2], aempty[2], bfull[2], bempty[2];
@@ -105,10 +111,16 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
     const int units = batch * bands;
     const int chunks = s / kChunk;
     const int dh = d / 64;  // d-halves (1 or 2)
-    // this CTA's units: blockIdx.x + i*gridDim.x, i < n
-    const int n = units > static_cast<int>(blockIdx.x)
-                      ? (units - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
-                      : 0;
+    // This CTA's units: runs of kRun consecutive bands of one batch, the runs
+    // dealt round-robin over the CTAs. Within a run pass 2 of unit i-1 and
+    // pass 1 of unit i read the same K (one load feeds both), while the CTAs
+    // together stay on a few batches at a time, so K and Q stay L2-resident.
+    const int run = (bands % kRun == 0) ? kRun : 1;
+    const int runs = units / run;
+    const int nruns = runs > static_cast<int>(blockIdx.x)
+                          ? (runs - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                          : 0;
+    const int n = nruns * run;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kKStages; ++i) {
@@ -121,11 +133,11 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
         }
         for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&sm.afull[i], 1);
-            tc::mbar_init(&sm.aempty[i], kGroupWarps);
+            tc::mbar_init(&sm.aempty[i], kAWarps);
             tc::mbar_init(&sm.bfull[i], 1);
-            tc::mbar_init(&sm.bempty[i], kGroupWarps);
-            tc::mbar_init(&sm.sfull[i], kGroupWarps);
-            tc::mbar_init(&sm.sempty[i], kGroupWarps);
+            tc::mbar_init(&sm.bempty[i], kBWarps);
+            tc::mbar_init(&sm.sfull[i], kAWarps);
+            tc::mbar_init(&sm.sempty[i], kBWarps);
         }
         sm.abort = 0;
         tc::fence_barrier_init();
@@ -138,7 +150,13 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
     const uint32_t tmem = sm.tmem_base;
     volatile int* abort = &sm.abort;
     auto unit_of = [&](int i) {
-        return static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+        return (static_cast<int>(blockIdx.x) + (i / run) * static_cast<int>(gridDim.x)) * run +
+               i % run;
+    };
+    // Step `step` (1 <= step < n) runs both passes on the same K chunks when
+    // units step-1 and step belong to the same batch: one load feeds both MMAs.
+    auto shares_k = [&](int step) {
+        return step > 0 && step < n && unit_of(step - 1) / bands == unit_of(step) / bands;
     };
 
     if (warp == 0 && lane == 0) {
@@ -182,8 +200,12 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
         const int qload_at = chunks > 1 ? 1 : 0;
         for (int step = 0; step <= n && ok; ++step) {
             for (int c = 0; c < chunks && ok; ++c) {
-                if (step > 0) ok = load_k(step - 1, c);   // pass 2 of unit step-1
-                if (ok && step < n) ok = load_k(step, c);  // pass 1 of unit step
+                if (shares_k(step)) {
+                    ok = load_k(step, c);  // both passes
+                } else {
+                    if (step > 0) ok = load_k(step - 1, c);   // pass 2 of unit step-1
+                    if (ok && step < n) ok = load_k(step, c);  // pass 1 of unit step
+                }
                 if (ok && c == qload_at && step + 1 < n && step + 1 >= 2) ok = load_q(step + 1);
             }
         }
@@ -215,6 +237,34 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
             }
             return true;
         };
+        // Both passes of a chunk from one K stage: pass 2 of unit step-1 into
+        // `db` (Q slot qb) and pass 1 of unit step into `da` (Q slot qa).
+        auto mma_chunk2 = [&](int qb, uint32_t db, int qa, uint32_t da) -> bool {
+            for (int h = 0; h < dh; ++h, ++kit) {
+                const int st = static_cast<int>(kit % kKStages);
+                if (!tc::mbar_wait(&sm.kfull[st], (kit / kKStages) & 1u, abort, kLimitNs)) {
+                    return false;
+                }
+                tc::tc_fence_after();
+                const uint32_t k0 = tc::smem_u32(sm.k[st]);
+                const uint32_t qb0 = tc::smem_u32(sm.q[qb][h]);
+                const uint32_t qa0 = tc::smem_u32(sm.q[qa][h]);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    tc::mma_f16(db, tc::smem_desc_sw128(qb0 + kk * 32, 16, 1024),
+                                tc::smem_desc_sw128(k0 + kk * 32, 16, 1024), kIdesc,
+                                (h > 0 || kk > 0) ? 1u : 0u);
+                }
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    tc::mma_f16(da, tc::smem_desc_sw128(qa0 + kk * 32, 16, 1024),
+                                tc::smem_desc_sw128(k0 + kk * 32, 16, 1024), kIdesc,
+                                (h > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc::mma_commit(&sm.kempty[st]);
+            }
+            return true;
+        };
         for (int step = 0; step <= n; ++step) {
             if (step < n &&
                 !tc::mbar_wait(&sm.qfull[step % kQSlots], (step / kQSlots) & 1, abort, kLimitNs)) {
@@ -222,7 +272,24 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
             }
             tc::tc_fence_after();
             bool ok = true;
+            const bool shared = shares_k(step);
             for (int c = 0; c < chunks && ok; ++c) {
+                if (shared) {  // both passes from the same K stages
+                    const uint32_t accb = bit & 1u, acca = ait & 1u;
+                    ok = tc::mbar_wait(&sm.bempty[accb], ((bit >> 1) & 1u) ^ 1u, abort, kLimitNs);
+                    ok = ok &&
+                         tc::mbar_wait(&sm.aempty[acca], ((ait >> 1) & 1u) ^ 1u, abort, kLimitNs);
+                    tc::tc_fence_after();
+                    ok = ok && mma_chunk2((step - 1) % kQSlots, tmem + 256 + accb * kChunk,
+                                          step % kQSlots, tmem + acca * kChunk);
+                    if (ok) {
+                        tc::mma_commit(&sm.bfull[accb]);
+                        tc::mma_commit(&sm.afull[acca]);
+                    }
+                    ++bit;
+                    ++ait;
+                    continue;
+                }
                 if (step > 0) {  // pass 2 of unit step-1 -> accumulators B (256, 384)
                     const uint32_t acc = bit & 1u;
                     ok = tc::mbar_wait(&sm.bempty[acc], ((bit >> 1) & 1u) ^ 1u, abort, kLimitNs);
@@ -244,11 +311,9 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
             // unit step-1 has had both passes: its Q slot is free once they finish
             if (step > 0) tc::mma_commit(&sm.qempty[(step - 1) % kQSlots]);
         }
-    } else if (warp >= 2 && warp < 2 + kGroupWarps) {
+    } else if (warp >= 2 && warp < 2 + kAWarps) {
         // ---------------- group A: pass 1 (row statistics) ----------------
-        const int ew = warp - 2;
         const int quarter = warp & 3;  // TMEM lanes this warp may read
-        const int part = ew >> 2;      // which 64 columns of a chunk
         const int row = quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         uint32_t ait = 0;
@@ -258,49 +323,56 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                 const uint32_t acc = ait & 1u;
                 if (!tc::mbar_wait(&sm.afull[acc], (ait >> 1) & 1u, abort, kLimitNs)) goto a_done;
                 tc::tc_fence_after();
-                uint32_t r[2][32];
-                const uint32_t col = lane_addr + acc * kChunk + part * 64;
-                tc::tmem_ld32(tmem + col, r[0]);
-                tc::tmem_ld32(tmem + col + 32, r[1]);
-                tc::tmem_ld_wait();
-                tc::tc_fence_before();
-                warp_arrive(&sm.aempty[acc], lane);  // values are in registers now
-                float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+                for (int h = 0; h < 2; ++h) {  // the chunk's two 64-column halves
+                    uint32_t r[2][32];
+                    const uint32_t col = lane_addr + acc * kChunk + h * 64;
+                    tc::tmem_ld32(tmem + col, r[0]);
+                    tc::tmem_ld32(tmem + col + 32, r[1]);
+                    tc::tmem_ld_wait();
+                    if (h == 1) {
+                        tc::tc_fence_before();
+                        warp_arrive(&sm.aempty[acc], lane);  // values are in registers now
+                    }
+                    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int j = 0; j < 64; j += 2) {
-                    mx[(j >> 1) & 3] = max3(mx[(j >> 1) & 3], __uint_as_float(r[j >> 5][j & 31]),
-                                            __uint_as_float(r[j >> 5][(j & 31) + 1]));
-                }
-                const float gm = max3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * c2;
-                const float mn = fmaxf(m, gm);
-                // exponent arguments and partial sums two at a time (packed f32x2)
-                float2 sum[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+                    for (int j = 0; j < 64; j += 2) {
+                        mx[(j >> 1) & 3] =
+                            max3(mx[(j >> 1) & 3], __uint_as_float(r[j >> 5][j & 31]),
+                                 __uint_as_float(r[j >> 5][(j & 31) + 1]));
+                    }
+                    const float gm = max3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * c2;
+                    const float mn = fmaxf(m, gm);
+                    // exponent arguments and partial sums two at a time (packed f32x2)
+                    float2 sum[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
 #pragma unroll
-                for (int j = 0; j < 64; j += 2) {
-                    const float2 t = __ffma2_rn(make_float2(__uint_as_float(r[j >> 5][j & 31]),
-                                                            __uint_as_float(r[j >> 5][(j & 31) + 1])),
-                                                make_float2(c2, c2), make_float2(-mn, -mn));
-                    sum[(j >> 1) & 1] =
-                        __fadd2_rn(sum[(j >> 1) & 1], make_float2(ex2(t.x), ex2(t.y)));
+                    for (int j = 0; j < 64; j += 2) {
+                        const float2 t =
+                            __ffma2_rn(make_float2(__uint_as_float(r[j >> 5][j & 31]),
+                                                   __uint_as_float(r[j >> 5][(j & 31) + 1])),
+                                       make_float2(c2, c2), make_float2(-mn, -mn));
+                        sum[(j >> 1) & 1] =
+                            __fadd2_rn(sum[(j >> 1) & 1], make_float2(ex2(t.x), ex2(t.y)));
+                    }
+                    l = l * ex2(m - mn) + ((sum[0].x + sum[0].y) + (sum[1].x + sum[1].y));
+                    m = mn;
                 }
-                l = l * ex2(m - mn) + ((sum[0].x + sum[0].y) + (sum[1].x + sum[1].y));
-                m = mn;
             }
-            // hand (max, sum) of this part of the row to group B
+            // hand (max, sum) of the row to group B
             {
                 const int slot = i & 1;
                 if (i >= 2 &&
                     !tc::mbar_wait(&sm.sempty[slot], ((i >> 1) - 1) & 1, abort, kLimitNs)) {
                     goto a_done;
                 }
-                sm.stats[slot][part][row] = make_float2(m, l);
+                sm.stats[slot][row] = make_float2(m, l);
                 warp_arrive(&sm.sfull[slot], lane);
             }
         }
     a_done:;
-    } else if (warp >= 2 + kGroupWarps) {
+    } else if (warp >= 2 + kAWarps) {
         // ---------------- group B: pass 2 (normalised write) ----------------
-        const int ew = warp - 2 - kGroupWarps;
+        const int ew = warp - 2 - kAWarps;
         const int quarter = warp & 3;
         const int part = ew >> 2;
         const int row = quarter * 32 + lane;
@@ -315,10 +387,9 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
             {
                 const int slot = i & 1;
                 if (!tc::mbar_wait(&sm.sfull[slot], (i >> 1) & 1, abort, kLimitNs)) goto b_done;
-                const float2 s0 = sm.stats[slot][0][row], s1 = sm.stats[slot][1][row];
+                const float2 st = sm.stats[slot][row];
                 warp_arrive(&sm.sempty[slot], lane);
-                const float m = fmaxf(s0.x, s1.x);
-                const float l = s0.y * ex2(s0.x - m) + s1.y * ex2(s1.x - m);
+                const float m = st.x, l = st.y;
                 // +inf score: the reference's exp(inf - inf) poisons the row
                 mi = (m == INFINITY) ? __int_as_float(0x7fffffff) : m + log2f(l);
             }
@@ -330,15 +401,10 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                 tc::tc_fence_after();
                 const uint32_t col = lane_addr + 256 + acc * kChunk + part * 64;
                 float* const ydst0 = yband + c * kChunk + part * 64;
-#pragma unroll 1
-                for (int g = 0; g < 2; ++g) {
-                    uint32_t r[32];
-                    tc::tmem_ld32(tmem + col + g * 32, r);
-                    tc::tmem_ld_wait();
-                    if (g == 1) {
-                        tc::tc_fence_before();
-                        warp_arrive(&sm.bempty[acc], lane);
-                    }
+                // One 32-column group: exponentials, swizzled staging, transposed
+                // stores (8 lanes per row, 4 rows per instruction, every store a
+                // full 128-byte row segment).
+                auto write_group = [&](const uint32_t (&r)[32], int g) {
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
                         // exponent arguments two at a time (packed f32x2 FMA)
@@ -357,8 +423,6 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                         *reinterpret_cast<float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4)) = v;
                     }
                     __syncwarp();
-                    // transpose through the tile: 8 lanes per row, 4 rows per
-                    // instruction, every store a full 128-byte row segment
 #pragma unroll
                     for (int t = 0; t < 8; ++t) {
                         const int rr = t * 4 + (lane >> 3);
@@ -369,7 +433,16 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                                v);
                     }
                     __syncwarp();
-                }
+                };
+                uint32_t r0[32], r1[32];
+                tc::tmem_ld32(tmem + col, r0);
+                tc::tmem_ld_wait(r0);
+                tc::tmem_ld32(tmem + col + 32, r1);  // in flight while group 0 is written
+                write_group(r0, 0);
+                tc::tmem_ld_wait(r1);
+                tc::tc_fence_before();
+                warp_arrive(&sm.bempty[acc], lane);
+                write_group(r1, 1);
             }
         }
     b_done:;

@@ -66,14 +66,34 @@ __device__ __forceinline__ float flip_if(float v, int q) {
     return __uint_as_float(__float_as_uint(v) ^ ((static_cast<uint32_t>(q) << 30) & 0x80000000u));
 }
 
+// sin alone reduces by pi instead of pi/2: sin(u) = (-1)^k sin(r) with
+// r = u - k*pi in [-pi/2, pi/2] (two-term pi, the first FMA term exact as
+// above), and one odd polynomial r + r^3 S(r^2) of degree 9 on that range
+// (near-minimax, relative error < 6.2e-9) serves every k: no quadrant select.
+__device__ __forceinline__ double sin_half_period(double u, int& k) {
+    const double kInvPi = 0.3183098861837907;        // fl64(1/pi)
+    const double kPiHi = 3.141592653589793;          // fl64(pi)
+    const double kPiLo = 1.2246467991473532e-16;     // fl64(pi - kPiHi)
+    const double kMagic = 6755399441055744.0;        // 1.5 * 2^52
+    const double t = fma(u, kInvPi, kMagic);
+    const double kd = t - kMagic;
+    k = __double2loint(t);
+    const double r = fma(-kd, kPiLo, fma(-kd, kPiHi, u));
+    const double z = r * r;
+    double p = fma(z, 2.6054811598334154e-06, -0.00019809474742454904);
+    p = fma(z, p, 0.008333064608556094);
+    p = fma(z, p, -0.1666665949166532);
+    return fma(r * z, p, r);
+}
+
 struct SinOp {
     static constexpr int kOuts = 1;
     __device__ __forceinline__ static void fast(float x, float& y0, float&) {
-        int q;
-        const double r = dev::reduce_pio2(u_of(x), q);
-        const double z = r * r;
-        const double v = (q & 1) ? cos_r(z) : sin_r(r, z);
-        y0 = flip_if(static_cast<float>(v), q);
+        int k;
+        const double v = sin_half_period(u_of(x), k);
+        // (-1)^k: bit 0 of k into the sign bit of the rounded result
+        y0 = __uint_as_float(__float_as_uint(static_cast<float>(v)) ^
+                             (static_cast<uint32_t>(k) << 31));
     }
     __device__ __noinline__ static float2 slow(float x) {
         return make_float2(static_cast<float>(dev::sin_f64(u_of(x))), 0.0f);

@@ -22,11 +22,11 @@
 //   warps 2-5    group A (pass 1), one warp per TMEM lane quarter: online row
 //                max / sum of exp2(scale*log2e*s), handed to group B through a
 //                double-buffered statistics slot;
-//   warps 6-13   group B (pass 2), two warps per lane quarter: recompute,
+//   warps 6-17   group B (pass 2), three warps per lane quarter sharing each
+//                chunk's four 32-column groups round-robin: recompute,
 //                exp2(s*c - (m + log2 l)), transpose through an XOR-swizzled
 //                shared-memory tile so every global store is a full 128-byte
-//                row segment; the TMEM load of a warp's second 32-column group
-//                is in flight while its first is written.
+//                row segment.
 // Every mbarrier wait is bounded (2 s); on a timeout the CTA raises the
 // device status word, drains its copies, frees TMEM and returns.
 // Other shapes use the two-step form (tcgen05 GEMM with the scale folded into
@@ -55,15 +55,15 @@ constexpr int kQSlots = 3;   // Q bands resident: units i-1, i and the prefetche
 constexpr uint32_t kKBox = kChunk * 64 * 2;  // 16 KB
 constexpr uint32_t kQBox = kRows * 64 * 2;   // 16 KB (one d-half)
 constexpr int kAWarps = 4;                   // pass 1: one warp per lane quarter
-constexpr int kBWarps = 8;                   // pass 2: two warps per lane quarter
-constexpr int kThreads = 64 + (kAWarps + kBWarps) * 32;  // 448
+constexpr int kBWarps = 12;                  // pass 2: three warps per lane quarter
+constexpr int kThreads = 64 + (kAWarps + kBWarps) * 32;  // 576
 constexpr uint32_t kStageTile = 32 * 32 * 4;         // [32 rows x 32 cols] f32
 constexpr uint64_t kLimitNs = 2000000000ull;
 
 struct QkSmem {
     uint8_t k[kKStages][kKBox];              // 80 KB
     uint8_t q[kQSlots][2][kQBox];            // 96 KB
-    uint8_t out[kBWarps][kStageTile];        // 32 KB (group B staging)
+    uint8_t out[kBWarps][kStageTile];        // 48 KB (group B staging)
     float2 stats[2][kRows];                  // [slot][row] = (max, sum)
     uint64_t kfull[kKStages], kempty[kKStages];
     uint64_t qfull[kQSlots], qempty[kQSlots];
@@ -374,7 +374,7 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
         // ---------------- group B: pass 2 (normalised write) ----------------
         const int ew = warp - 2 - kAWarps;
         const int quarter = warp & 3;
-        const int part = ew >> 2;
+        const int sub = ew >> 2;  // 0..2: which of the quarter's three warps
         const int row = quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         uint8_t* const tile = sm.out[ew];
@@ -399,8 +399,12 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                 const uint32_t acc = bit & 1u;
                 if (!tc::mbar_wait(&sm.bfull[acc], (bit >> 1) & 1u, abort, kLimitNs)) goto b_done;
                 tc::tc_fence_after();
-                const uint32_t col = lane_addr + 256 + acc * kChunk + part * 64;
-                float* const ydst0 = yband + c * kChunk + part * 64;
+                // The chunk's four 32-column groups, numbered 4*bit + g over the
+                // whole run, are dealt round-robin to the quarter's three warps:
+                // this warp takes one or two of them.
+                const int g0 = (sub - static_cast<int>((4u * bit) % 3u) + 3) % 3;  // first g of ours
+                const int g1 = g0 + 3;                                          // second, if < 4
+                float* const ydst0 = yband + c * kChunk;
                 // One 32-column group: exponentials, swizzled staging, transposed
                 // stores (8 lanes per row, 4 rows per instruction, every store a
                 // full 128-byte row segment).
@@ -434,15 +438,16 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                     }
                     __syncwarp();
                 };
+                const uint32_t col = lane_addr + 256 + acc * kChunk;
                 uint32_t r0[32], r1[32];
-                tc::tmem_ld32(tmem + col, r0);
+                tc::tmem_ld32(tmem + col + g0 * 32, r0);
+                if (g1 < 4) tc::tmem_ld32(tmem + col + g1 * 32, r1);
                 tc::tmem_ld_wait(r0);
-                tc::tmem_ld32(tmem + col + 32, r1);  // in flight while group 0 is written
-                write_group(r0, 0);
-                tc::tmem_ld_wait(r1);
+                if (g1 < 4) tc::tmem_ld_wait(r1);
                 tc::tc_fence_before();
-                warp_arrive(&sm.bempty[acc], lane);
-                write_group(r1, 1);
+                warp_arrive(&sm.bempty[acc], lane);  // values are in registers now
+                write_group(r0, g0);
+                if (g1 < 4) write_group(r1, g1);
             }
         }
     b_done:;

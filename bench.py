@@ -113,9 +113,11 @@ class ClockSampler:
                 "samples": len(sms)}
 
 
-def cpu_reference_map2(n_sample: int, steps: int):
+def cpu_reference_map2(n_sample: int, steps: int, default_threads: bool = False):
     """The reference's own executor (or the C port) on a bounded sample of
-    the config-2 workload, all host threads. Returns (GB/s, kind, cores, secs)."""
+    the config-2 workload, all host threads (or, with default_threads, the
+    executor's own default of at most 4 threads, kernel_buffers.cpp:183-199).
+    Returns (GB/s, kind, cores, secs)."""
     import numpy as np
 
     import oracle
@@ -126,7 +128,10 @@ def cpu_reference_map2(n_sample: int, steps: int):
     chains = [kir.SIN_CHAIN, kir.DSIN_CHAIN]
     if oracle.ref_available():
         ex, kind = oracle.ref(), "reference"
-        run = lambda: ex.chain(chains, x, threads=cores)  # noqa: E731
+        if default_threads:
+            cores = min(cores, 4)
+        thr = 0 if default_threads else cores
+        run = lambda: ex.chain(chains, x, threads=thr)  # noqa: E731
     else:
         ex, kind, cores = oracle.port(), "port", 1
         run = lambda: ex.chain(chains, x)  # noqa: E731
@@ -138,6 +143,79 @@ def cpu_reference_map2(n_sample: int, steps: int):
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
     return n_sample * BYTES_PER_ELEM_MAP2 / t / 1e9, kind, cores, t
+
+
+def cpu_reference_configs(reps: int = 3):
+    """The reference's executor (or the C port) on bounded samples of configs
+    1, 3, 4, 4' and 5, timed on this host beside the GPU numbers. Bytes are
+    counted at the GPU path's storage width, as the GPU rows are."""
+    import numpy as np
+
+    import oracle
+    from mlk2_b200 import kir
+
+    cores = os.cpu_count() or 1
+    have_ref = oracle.ref_available()
+    ex, kind = (oracle.ref(), "reference") if have_ref else (oracle.port(), "port")
+    thr = cores if have_ref else 1
+
+    def timed(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+    rng = np.random.default_rng(SEED)
+    out = {}
+    # config 1: the whole workload (2^24 elements)
+    n1 = 1 << 24
+    x1 = oracle.fill_uniform_f32(n1, SEED, 1, -4.0, 4.0).astype(np.float64)
+    t = timed(lambda: ex.chain([kir.SIN_CHAIN], x1, threads=thr))
+    out["map1"] = {"value": n1 * 8 / t / 1e9, "unit": "GB/s", "cores": thr, "kind": kind,
+                   "sample": "the full 2^24-element config 1, f64 arithmetic, bytes at f32 "
+                             "width (8 B/element)"}
+    # config 3: 1024 of the 65536 rows (Call(Softmax) is single-threaded)
+    xs = (rng.standard_normal((1024, 4096)) * 4.0).astype(np.float32).astype(np.float64)
+    t = timed(lambda: ex.softmax(xs))
+    out["softmax"] = {"value": xs.size * 8 / t / 1e9, "unit": "GB/s", "cores": 1,
+                      "kind": kind, "sample": "1024 rows x 4096 of config 3 (the reference's "
+                                              "softmax runs on one thread), bytes at 8 B/elem"}
+    # config 4: a 64-row M sample of the 8192^3 GEMM, extrapolated linearly in M
+    a = (rng.standard_normal((64, 8192), dtype=np.float32) / 90.50966799187809)
+    b = (rng.standard_normal((8192, 8192), dtype=np.float32) / 90.50966799187809)
+    a = a.astype(np.float16).astype(np.float64)
+    b = b.astype(np.float16).astype(np.float64)
+    t = timed(lambda: ex.matmul(a, b, threads=thr)) if reps else 0.0
+    out["gemm_f16"] = {"value": 2.0 * 64 * 8192 * 8192 / t / 1e12, "unit": "TFLOP/s",
+                       "cores": thr, "kind": kind,
+                       "sample": "64 of 8192 rows of A (f16 values widened to f64), full B; "
+                                 "TFLOP/s extrapolated linearly in M"}
+    del b
+    # config 4': the whole 1024^3 f32 GEMM (in f64)
+    a = rng.standard_normal((1024, 1024)).astype(np.float32).astype(np.float64) / 32
+    b = rng.standard_normal((1024, 1024)).astype(np.float32).astype(np.float64) / 32
+    t = timed(lambda: ex.matmul(a, b, threads=thr))
+    out["gemm_f32_1024"] = {"value": 2.0 * 1024 ** 3 / t / 1e12, "unit": "TFLOP/s",
+                            "cores": thr, "kind": kind, "sample": "the full 1024^3 GEMM"}
+    # config 5: one 128-row band of one batch (MatMul -> scale map -> Softmax)
+    q = rng.standard_normal((128, 128)).astype(np.float16).astype(np.float64)
+    kt = rng.standard_normal((2048, 128)).astype(np.float16).astype(np.float64).T.copy()
+    mul = kir.chain(kir.E("mul", kir.A, kir.C(128 ** -0.5)))
+
+    def qk_band():
+        sc = ex.matmul(q, kt, threads=thr)
+        (sv,) = ex.chain([mul], sc.ravel(), threads=thr)
+        ex.softmax(sv.reshape(sc.shape))
+    t = timed(qk_band)
+    band_bytes = (2 * 256 * 2048 * 128 * 2 + 256 * 2048 * 2048 * 4) / (256 * 16)
+    out["qk_softmax"] = {"value": band_bytes / t / 1e9, "unit": "GB/s", "cores": thr,
+                         "kind": kind, "sample": "one 128-row band of one batch (K^T "
+                                                 "materialised, as the reference requires); "
+                                                 "GB/s at the GPU path's bytes per band"}
+    return out
 
 
 def run_reference_arm(args, rank):
@@ -318,6 +396,14 @@ def main():
         cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind,
                "sample": "2^24 elements of config 2 per run (median of 3), f64 arithmetic, "
                          "bytes counted at f32 width (12 B/element)"}
+        if kind == "reference":
+            vd, _, cd, _ = cpu_reference_map2(1 << 24, 3, default_threads=True)
+            cpu["default_executor"] = {"value": vd, "cores": cd,
+                                       "note": "the executor's default schedule (<= 4 threads)"}
+        if configs:
+            for name, base in cpu_reference_configs().items():
+                if name in configs:
+                    configs[name]["cpu_baseline"] = base
 
     if rank == 0:
         line = {

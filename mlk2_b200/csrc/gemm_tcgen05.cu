@@ -241,12 +241,14 @@ gemm_f16_tcgen05(const __grid_constant__ CUtensorMap tma_a,
 // Both CTAs' TMA loads complete on the even CTA's `full` barrier; the MMA
 // commit multicasts stage release and accumulator-ready to both CTAs; both
 // epilogues report a drained accumulator on the even CTA's `tempty`.
-constexpr int kPairStages = 6;
-constexpr uint32_t kBHalf = kBK * (kBN / 2) * 2;  // 16 KB: [64 K-rows x 128 N]
+constexpr int kPairBK = 128;                         // K per stage: two 64-wide halves
+constexpr int kPairStages = 3;
+constexpr uint32_t kPairA = kBM * kPairBK * 2;             // 32 KB: two [128 x 64] boxes
+constexpr uint32_t kPairB = kPairBK * (kBN / 2) * 2;       // 32 KB: 2 K-halves x 2 N-boxes
 
 struct PairSmem {
-    uint8_t a[kPairStages][kAStage];
-    uint8_t b[kPairStages][kBHalf];
+    uint8_t a[kPairStages][kPairA];
+    uint8_t b[kPairStages][kPairB];
     uint64_t full[kPairStages];
     uint64_t empty[kPairStages];
     uint64_t tfull[2];
@@ -269,7 +271,7 @@ gemm_f16_tcgen05_pair(const __grid_constant__ CUtensorMap tma_a,
     const bool leader = (rank == 0);
     const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
     const int mt = (m + 2 * kBM - 1) / (2 * kBM), nt = (n + kBN - 1) / kBN;
-    const int kt = (k + kBK - 1) / kBK;
+    const int kt = (k + kPairBK - 1) / kPairBK;
     const int tiles = mt * nt;
 
     if (threadIdx.x == 0) {
@@ -307,11 +309,15 @@ gemm_f16_tcgen05_pair(const __grid_constant__ CUtensorMap tma_a,
                 const int st = static_cast<int>(it % kPairStages);
                 const uint32_t ph = (it / kPairStages) & 1u;
                 if (!tc::mbar_wait(&s.empty[st], ph ^ 1u, abort, kWaitLimitNs)) goto producer_done;
-                if (leader) tc::mbar_arrive_expect_tx(&s.full[st], 2 * (kAStage + kBHalf));
+                if (leader) tc::mbar_arrive_expect_tx(&s.full[st], 2 * (kPairA + kPairB));
                 const uint32_t bar = tc::mapa_shared(tc::smem_u32(&s.full[st]), 0);
-                tc::tma_load_2d_pair(s.a[st], &tma_a, bar, kb * kBK, arow);
-                tc::tma_load_2d_pair(s.b[st], &tma_b, bar, bcol, kb * kBK);
-                tc::tma_load_2d_pair(s.b[st] + kBBox, &tma_b, bar, bcol + 64, kb * kBK);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {  // K halves of the stage
+                    const int k0 = kb * kPairBK + h * 64;
+                    tc::tma_load_2d_pair(s.a[st] + h * kAStage, &tma_a, bar, k0, arow);
+                    tc::tma_load_2d_pair(s.b[st] + h * 2 * kBBox, &tma_b, bar, bcol, k0);
+                    tc::tma_load_2d_pair(s.b[st] + h * 2 * kBBox + kBBox, &tma_b, bar, bcol + 64, k0);
+                }
             }
         }
     producer_done:
@@ -340,9 +346,11 @@ gemm_f16_tcgen05_pair(const __grid_constant__ CUtensorMap tma_a,
                 const uint32_t a0 = tc::smem_u32(s.a[st]);
                 const uint32_t b0 = tc::smem_u32(s.b[st]);
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk) {
-                    const uint64_t ad = tc::smem_desc_sw128(a0 + kk * 32, 16, 1024);
-                    const uint64_t bd = tc::smem_desc_sw128(b0 + kk * 2048, kBBox, 1024);
+                for (int kk = 0; kk < kPairBK / 16; ++kk) {
+                    const uint32_t h = kk >> 2, q = kk & 3;  // K half, K16 step inside it
+                    const uint64_t ad = tc::smem_desc_sw128(a0 + h * kAStage + q * 32, 16, 1024);
+                    const uint64_t bd =
+                        tc::smem_desc_sw128(b0 + h * 2 * kBBox + q * 2048, kBBox, 1024);
                     tc::mma_f16_pair(d, ad, bd, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
                 }
                 tc::mma_commit_pair(&s.empty[st], 0x3);

@@ -31,8 +31,10 @@ constexpr int kMapUnroll = 2;  // float4 vectors per thread per step (plus a pre
 // relative error < 3.9e-9, cos r = 1 + r^2 C(r^2) with relative error
 // < 3.9e-8. An f32 result needs relative error below half an f32 ulp
 // (2^-25 = 3e-8 at worst, 6e-8 typically) for its rounding to land within one
-// ulp of the correctly rounded value; these stay there. cos(0) = 1 and
-// sin(r) = r for tiny r hold exactly.
+// ulp of the correctly rounded value; these stay there. (Degree 9/8 forms
+// round ~99.97 % of outputs exactly but cost ~5 % of this HBM-bound kernel's
+// time under the power cap, where the f64 pipe sets the clock.)
+// cos(0) = 1 and sin(r) = r for tiny r hold exactly.
 __device__ __forceinline__ double sin_r(double r, double z) {
     double p = fma(z, -0.0001951397821210659, 0.008332151315419242);
     p = fma(z, p, -0.16666654462992936);
@@ -144,6 +146,12 @@ template <class Op>
 __global__ void __launch_bounds__(kMapThreads)
 map_vec_kernel(const float4* __restrict__ x, float4* __restrict__ y0,
                float4* __restrict__ y1, int64_t nvec) {
+    // Launched with programmatic stream serialization: wait until the
+    // preceding grid in the stream has finished and its writes are visible,
+    // then let the next grid's blocks be scheduled as ours retire (it waits
+    // the same way), so back-to-back maps overlap launch and tail.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     constexpr int64_t kBlock = static_cast<int64_t>(kMapThreads) * kMapUnroll;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * kBlock;
     int64_t base = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
@@ -206,9 +214,19 @@ int launchMap(const float* x, float* y0, float* y1, int64_t n, void* stream) {
     int64_t done = 0;
     if (vec && n >= 4) {
         const int64_t nvec = n / 4;
-        map_vec_kernel<Op><<<gridFor(nvec, kMapThreads * kMapUnroll), kMapThreads, 0, s>>>(
-            reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y0),
-            reinterpret_cast<float4*>(y1), nvec);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(gridFor(nvec, kMapThreads * kMapUnroll));
+        cfg.blockDim = dim3(kMapThreads);
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t le = cudaLaunchKernelEx(
+            &cfg, map_vec_kernel<Op>, reinterpret_cast<const float4*>(x),
+            reinterpret_cast<float4*>(y0), reinterpret_cast<float4*>(y1), nvec);
+        if (le != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, le, "map kernel launch");
         done = nvec * 4;
     }
     if (done < n) {

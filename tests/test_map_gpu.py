@@ -88,6 +88,28 @@ def test_full_size_configs_sampled(cuda, cfg):
         assert oracle.ulp_f32(host(dy[::stride]), refs[1]).max() <= ULP_BOUND
 
 
+def test_fast_path_wide_sample(cuda):
+    """2^21 inputs over the whole fast-path range |x| < 1000 (where
+    |x^2 + 3x| reaches 10^6 and the reduction does real work) plus every
+    binade of small |x|: both specialised kernels within the bound of the
+    f64 oracle; the observed worst case and 1-ULP rate are printed."""
+    rng = np.random.default_rng(77)
+    n = 1 << 21
+    parts = [rng.uniform(-1000.0, 1000.0, n // 2),
+             rng.uniform(-8.0, 8.0, n // 4),
+             np.sign(rng.uniform(-1, 1, n // 4)) * 2.0 ** rng.uniform(-40, 9.9, n // 4)]
+    xh = np.concatenate(parts).astype(np.float32)
+    x = dev(cuda, xh)
+    y, dy, y1 = (empty(cuda, xh.shape, cuda.float32) for _ in range(3))
+    api.map_sin_dsin(x, y, dy)
+    api.map_sin(x, y1)
+    ry, rdy = oracle.port().chain([kir.SIN_CHAIN, kir.DSIN_CHAIN], xh.astype(np.float64))
+    for name, got, ref in (("sin_dsin.y", y, ry), ("sin_dsin.dy", dy, rdy), ("sin.y", y1, ry)):
+        d = oracle.ulp_f32(host(got), ref)
+        print(f"{name}: max {int(d.max())} ULP, {100.0 * np.mean(d > 0):.2f} % off by >= 1")
+        assert d.max() <= ULP_BOUND, (name, int(d.max()))
+
+
 ARITH = {"add", "sub", "mul", "div", "neg", "pow22", "scalar", "poly", "sqrt", "rsqrt"}
 
 

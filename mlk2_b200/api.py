@@ -115,10 +115,19 @@ class Module:
         check(lib().mlkb_module_create(text.encode(), C.byref(h)))
         self._h = h
 
-    def __del__(self):
+    def close(self) -> None:
+        """Releases the native module (also done when the object is collected)."""
         if getattr(self, "_h", None):
             lib().mlkb_module_destroy(self._h)
             self._h = None
+
+    def __del__(self):
+        # At interpreter shutdown the module globals this needs may already be
+        # gone; the process is exiting and the handle dies with it.
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass
 
     @property
     def kind(self) -> int:

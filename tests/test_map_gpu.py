@@ -110,6 +110,25 @@ def test_fast_path_wide_sample(cuda):
         assert d.max() <= ULP_BOUND, (name, int(d.max()))
 
 
+def test_back_to_back_dependent_maps(cuda):
+    """Map launches overlap through programmatic dependent launch; a map that
+    reads the previous map's output must still see all of it (each kernel
+    waits on the preceding grid before touching memory). 40 chained launches
+    over 2^24 elements, each the next one's input, against the same chain run
+    with a device synchronisation between launches."""
+    n = 1 << 24
+    x0 = dev(cuda, oracle.fill_uniform_f32(n, 11, 1, -4.0, 4.0))
+    bufs = [x0.clone(), cuda.empty_like(x0)]
+    for i in range(40):
+        api.map_sin(bufs[i & 1], bufs[(i + 1) & 1])
+    chained = host(bufs[0])
+    ref = [x0.clone(), cuda.empty_like(x0)]
+    for i in range(40):
+        api.map_sin(ref[i & 1], ref[(i + 1) & 1])
+        cuda.cuda.synchronize()
+    assert np.array_equal(chained, host(ref[0]))
+
+
 ARITH = {"add", "sub", "mul", "div", "neg", "pow22", "scalar", "poly", "sqrt", "rsqrt"}
 
 

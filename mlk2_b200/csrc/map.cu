@@ -24,7 +24,6 @@ namespace mlkb {
 namespace {
 
 constexpr int kMapThreads = 256;
-constexpr int kMapUnroll = 2;  // float4 vectors per thread per step (plus a prefetched step)
 
 // Near-minimax polynomials on |r| <= pi/4 (fitted for this library by
 // weighted least squares on Chebyshev nodes): sin r = r + r^3 S(r^2) with
@@ -88,8 +87,16 @@ __device__ __forceinline__ double sin_half_period(double u, int& k) {
     return fma(r * z, p, r);
 }
 
+// Per op: kUnroll float4 vectors per thread per step (plus a prefetched
+// step) and at most kBlocksPerSm blocks per SM in the grid. The two-output
+// map streams 12 B per element and wants more bytes in flight and many short
+// blocks the hardware can balance across SMs (measured on a 2^28 run: 4 and
+// 64 take it from 0.58 to 0.49 ms at full clock); the single-output map is
+// compute-heavier per byte and runs best with 2 and 8.
 struct SinOp {
     static constexpr int kOuts = 1;
+    static constexpr int kUnroll = 2;
+    static constexpr int kBlocksPerSm = 8;
     __device__ __forceinline__ static void fast(float x, float& y0, float&) {
         int k;
         const double v = sin_half_period(u_of(x), k);
@@ -104,6 +111,8 @@ struct SinOp {
 
 struct SinDsinOp {
     static constexpr int kOuts = 2;
+    static constexpr int kUnroll = 4;
+    static constexpr int kBlocksPerSm = 64;
     __device__ __forceinline__ static void fast(float x, float& y0, float& y1) {
         int q;
         const double r = dev::reduce_pio2(u_of(x), q);
@@ -139,7 +148,7 @@ __device__ __forceinline__ void eval4(float4 v, float4& o0, float4& o1) {
     }
 }
 
-// Vector body: each CTA strides over blocks of kMapThreads*kMapUnroll
+// Vector body: each CTA strides over blocks of kMapThreads*Op::kUnroll
 // float4; each thread keeps the next block's loads in flight while it
 // computes the current one. 16-byte aligned pointers only.
 template <class Op>
@@ -152,25 +161,25 @@ map_vec_kernel(const float4* __restrict__ x, float4* __restrict__ y0,
     // the same way), so back-to-back maps overlap launch and tail.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    constexpr int64_t kBlock = static_cast<int64_t>(kMapThreads) * kMapUnroll;
+    constexpr int64_t kBlock = static_cast<int64_t>(kMapThreads) * Op::kUnroll;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * kBlock;
     int64_t base = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
-    float4 cur[kMapUnroll];
+    float4 cur[Op::kUnroll];
 #pragma unroll
-    for (int u = 0; u < kMapUnroll; ++u) {
+    for (int u = 0; u < Op::kUnroll; ++u) {
         const int64_t i = base + u * kMapThreads;
         if (i < nvec) cur[u] = __ldcs(x + i);
     }
     for (; base < nvec; base += stride) {
-        float4 nxt[kMapUnroll];
+        float4 nxt[Op::kUnroll];
         const int64_t nb = base + stride;
 #pragma unroll
-        for (int u = 0; u < kMapUnroll; ++u) {
+        for (int u = 0; u < Op::kUnroll; ++u) {
             const int64_t i = nb + u * kMapThreads;
             if (i < nvec) nxt[u] = __ldcs(x + i);
         }
 #pragma unroll
-        for (int u = 0; u < kMapUnroll; ++u) {
+        for (int u = 0; u < Op::kUnroll; ++u) {
             const int64_t i = base + u * kMapThreads;
             if (i < nvec) {
                 float4 o0, o1;
@@ -196,9 +205,9 @@ __global__ void map_scalar_kernel(const float* __restrict__ x, float* __restrict
     }
 }
 
-int gridFor(int64_t work, int per_block) {
+int gridFor(int64_t work, int per_block, int blocks_per_sm = 8) {
     const int64_t blocks = (work + per_block - 1) / per_block;
-    const int64_t cap = static_cast<int64_t>(smCount()) * 8;
+    const int64_t cap = static_cast<int64_t>(smCount()) * blocks_per_sm;
     return static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
 }
 
@@ -215,7 +224,7 @@ int launchMap(const float* x, float* y0, float* y1, int64_t n, void* stream) {
     if (vec && n >= 4) {
         const int64_t nvec = n / 4;
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(gridFor(nvec, kMapThreads * kMapUnroll));
+        cfg.gridDim = dim3(gridFor(nvec, kMapThreads * Op::kUnroll, Op::kBlocksPerSm));
         cfg.blockDim = dim3(kMapThreads);
         cfg.stream = s;
         cudaLaunchAttribute attr[1];

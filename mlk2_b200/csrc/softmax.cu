@@ -84,8 +84,8 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint3
 
 constexpr uint64_t kRowWaitLimitNs = 2000000000ull;
 
-// Row softmax, persistent CTAs (6 per SM at 4096 columns): each CTA owns rows
-// blockIdx.x + i*gridDim.x.
+// Row softmax: each CTA owns rows blockIdx.x + i*gridDim.x (6 CTAs resident
+// per SM at 4096 columns, a grid of four such waves).
 // A TMA bulk copy brings row i+2 into a shared-memory double buffer while row
 // i is computed, so HBM reads stay in flight across the block reductions.
 // Two block barriers per row: one for the max (it also carries the vote on
@@ -322,7 +322,11 @@ int launchRowsTma(const float* x, float* y, int64_t rows, int64_t cols, cudaStre
         if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "softmax smem attribute");
         attr[dev] = true;
     }
-    const int per_sm = NV <= 2 ? 8 : NV <= 4 ? 6 : 3;
+    // Resident CTAs per SM are 8 / 6 / 3 (shared memory); the grid holds four
+    // times that, so each CTA streams ~18 rows at 65536 x 4096 and the
+    // hardware rebalances the short CTAs across SMs (6 % faster than one
+    // resident wave of persistent CTAs).
+    const int per_sm = 4 * (NV <= 2 ? 8 : NV <= 4 ? 6 : 3);
     softmax_rows_tma<NV, kFull><<<rowGrid(rows, per_sm), kRowThreads, smem, s>>>(
         x, y, rows, cols, deviceStatusPtr());
     return checkLaunch("softmax launch");

@@ -6,12 +6,13 @@
 //   e = exp(x - r); s = sum e          NaN anywhere poisons the whole row
 //   y = (s != 0) ? e / s : 0
 //
-// f32 path (the BASELINE config, HBM-bound, 8 B per element): one CTA per
-// row, the row held in registers after ONE coalesced float4 read; the max in
-// f32 (exact), x - r and exp in f64, the sum in f64, and y = e * (1/s)
-// rounded once to f32. Rows that do not fit the register tile (or are not
-// float4-aligned) take a three-pass streaming kernel with the same
-// arithmetic.
+// f32 path (the BASELINE config, HBM-bound, 8 B per element): a 256-thread
+// CTA works one row at a time (rows blockIdx.x + i*gridDim.x), the row
+// brought into shared memory by one TMA bulk copy two rows ahead and then
+// held in registers; the max in f32 (exact), x - r and exp in f64, the sum
+// in f64, and y = e * (1/s) rounded once to f32: read once, write once.
+// Rows that do not fit the register tile (or are not float4-aligned) take a
+// three-pass streaming kernel with the same arithmetic.
 #include "common.cuh"
 #include "tc_common.cuh"
 

@@ -12,7 +12,7 @@
 //   4. runs the same module through mlk::executeKernelOnBuffers
 //      (runtime/src/execution/kernel_buffers.cpp:839) and prints the largest
 //      f64 ULP distance between the two, one JSON line per case.
-// Exit status: 0 when every case ran (the test judges the distances).
+// Exit status: 0 when every case ran (the calling test checks the distances).
 #include <dlfcn.h>
 
 #include <cmath>

@@ -84,30 +84,6 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src,
-                                             int32_t x, int32_t y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-            reinterpret_cast<uint64_t>(map)),
-        "r"(smem_u32(smem_src)), "r"(x), "r"(y)
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_store_commit() {
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-
-// Wait until at most N committed store groups still READ shared memory.
-template <int N>
-__device__ __forceinline__ void tma_store_wait_read() {
-    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-
-template <int N>
-__device__ __forceinline__ void tma_store_wait_all() {
-    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
-}
-
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

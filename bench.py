@@ -241,6 +241,29 @@ def run_reference_arm(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def _ulp_f32(torch, got, ref64):
+    """Ordered-bits ULP distance between f32 results and f64 references
+    rounded to f32 (NaN pairs count 0, +0 and -0 equal)."""
+    g = got.float().contiguous().view(torch.int32).to(torch.int64)
+    r = ref64.float().contiguous().view(torch.int32).to(torch.int64)
+    g = torch.where(g < 0, -2147483648 - g, g)
+    r = torch.where(r < 0, -2147483648 - r, r)
+    d = (g - r).abs()
+    both_nan = torch.isnan(got.float()) & torch.isnan(ref64)
+    return torch.where(both_nan, torch.zeros_like(d), d)
+
+
+def parity_gate(torch, name, got, ref64, ulp_bound=None, rel_bound=None, abs_floor=0.0):
+    """Checks a sample of a config's output against a torch f64 recomputation
+    (the CUDA result is what is checked; torch only recomputes the formula)."""
+    if ulp_bound is not None:
+        worst = int(_ulp_f32(torch, got, ref64).max().item())
+        return {"check": f"{name}: <= {ulp_bound} ULP vs f64", "worst_ulp": worst,
+                "pass": worst <= ulp_bound}
+    err = ((got.double() - ref64).abs() / (ref64.abs() + abs_floor)).max().item()
+    return {"check": f"{name}: rel err <= {rel_bound}", "worst_rel": err, "pass": err <= rel_bound}
+
+
 def time_device(torch, fn, warmup, steps, dist, world, min_warm_s=0.0):
     """W untimed steps (continued until min_warm_s has passed, so clock samples
     see the same steady load), then K steps between barrier+sync; CUDA events
@@ -322,6 +345,13 @@ def main():
     y = torch.empty_like(x)
     dy = torch.empty_like(x)
     step = lambda: api.map_sin_dsin(x, y, dy)  # noqa: E731
+    step()  # parity gate before timing: every 4096th element against f64
+    xs_, us_ = x[::4096].double(), None
+    us_ = xs_ * xs_ + 3.0 * xs_
+    gate = {"y": parity_gate(torch, "sin(x^2+3x)", y[::4096], torch.sin(us_), ulp_bound=2),
+            "dy": parity_gate(torch, "cos(x^2+3x)(2x+3)", dy[::4096],
+                              torch.cos(us_) * (2.0 * xs_ + 3.0), ulp_bound=2)}
+    del xs_, us_
     with ClockSampler(local) as clk:
         sec = time_device(torch, step, args.warmup, args.steps, dist, world,
                           min_warm_s=args.min_warm_s)
@@ -417,7 +447,8 @@ def main():
                        "elements_per_gpu": n, "global_elements": n * world,
                        "parallelism": f"dp{world} (contiguous element shards)",
                        "l2": "inputs 1 GiB per GPU > 126 MB L2, no flush"},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gather": gather,
+            "roofline": roofline, "parity": gate, "cpu_baseline": cpu, "e2e": e2e,
+            "gather": gather,
             "gpu_launches": args.steps + sum(c.get("gpu_launches", 0) for c in configs.values()),
             "clocks": clocks, "configs": configs, "library": mb.version(),
         }
@@ -497,17 +528,26 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
         i = turn[0] % nsets
         turn[0] += 1
         api.map_sin(xs1[i], ys1[i])
+    api.map_sin(xs1[0], ys1[0])
+    x64 = xs1[0][::1024].double()
+    g1 = parity_gate(torch, "sin(x^2+3x)", ys1[0][::1024], torch.sin(x64 * x64 + 3.0 * x64),
+                     ulp_bound=2)
     sec = time_device(torch, step1, warm, steps, dist, world)
     rec("map1", sec, n1 * 8, "GB/s", "hbm", peaks["hbm_gbs"], 1,
-        {"note": "steps rotate over 8 input/output pairs (1 GiB > L2), no flush"})
+        {"note": "steps rotate over 8 input/output pairs (1 GiB > L2), no flush",
+         "parity": g1})
     del xs1, ys1
 
     # config 3: softmax [65536 x 4096] f32 per GPU
     xs = torch.empty((65536, 4096), device="cuda")
     api.fill(xs, SEED, 3 + 256 * rank, "normal", 0.0, 4.0)
     ys = torch.empty_like(xs)
+    api.softmax(xs, ys)
+    g3 = parity_gate(torch, "softmax rows", ys[::1024],
+                     torch.softmax(xs[::1024].double(), dim=1), ulp_bound=2)
     sec = time_device(torch, lambda: api.softmax(xs, ys), warm, steps, dist, world)
-    rec("softmax", sec, 2 * 4 * 65536 * 4096, "GB/s", "hbm", peaks["hbm_gbs"], 1)
+    rec("softmax", sec, 2 * 4 * 65536 * 4096, "GB/s", "hbm", peaks["hbm_gbs"], 1,
+        {"parity": g3})
     del xs, ys
 
     # config 4: GEMM 8192^3 f16 -> f32 (M-block shard per GPU in weak scaling)
@@ -517,18 +557,32 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     api.fill(a, SEED, 41 + 256 * rank, "normal", 0.0, n4 ** -0.5)
     api.fill(b, SEED, 42, "normal", 0.0, n4 ** -0.5)
     c = torch.empty((n4, n4), device="cuda")
+    api.gemm(a, b, c)
+    rows = slice(0, n4, 128)
+    ref4 = a[rows].double() @ b.double()
+    mag4 = a[rows].double().abs() @ b.double().abs()
+    err4 = ((c[rows].double() - ref4).abs() / mag4).max().item()
+    g4 = {"check": "f16 GEMM: |C - C_f64| <= 2^-12 sum|a b| (every 128th row)",
+          "worst": err4, "pass": err4 <= 2.0 ** -12}
+    del ref4, mag4
     sec = time_device(torch, lambda: api.gemm(a, b, c), warm, steps, dist, world)
     rec("gemm_f16", sec, 2.0 * n4 ** 3, "TFLOP/s", "tensor", peaks["bf16_tflops"], 1,
-        {"peak_note": "peak = measured cuBLAS bf16 dense burst (f16 has the same rate)"})
+        {"peak_note": "peak = measured cuBLAS bf16 dense burst (f16 has the same rate)",
+         "parity": g4})
     del a, b, c
 
     # config 4': GEMM 1024^3 f32 (SIMT FMA)
     a = torch.randn((1024, 1024), device="cuda") / 32
     b = torch.randn((1024, 1024), device="cuda") / 32
     c = torch.empty((1024, 1024), device="cuda")
+    api.gemm(a, b, c)
+    err5 = ((c.double() - a.double() @ b.double()).abs() /
+            (a.double().abs() @ b.double().abs())).max().item()
+    g5 = {"check": "f32 GEMM: |C - C_f64| <= 2^-14 sum|a b|", "worst": err5,
+          "pass": err5 <= 2.0 ** -14}
     sec = time_device(torch, lambda: api.gemm(a, b, c), warm, steps, dist, world)
     rec("gemm_f32_1024", sec, 2.0 * 1024 ** 3, "TFLOP/s", "fp32-simt", 80.0, 1,
-        {"peak_note": "nominal FP32 SIMT 80 TFLOP/s (context only)"})
+        {"peak_note": "nominal FP32 SIMT 80 TFLOP/s (context only)", "parity": g5})
     del a, b, c
 
     # config 5: batched Q K^T * s + softmax, 256 x [2048 x 2048], d = 128
@@ -538,10 +592,15 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     api.fill(q, SEED, 51 + 256 * rank, "normal", 0.0, 1.0)
     api.fill(k, SEED, 52 + 256 * rank, "normal", 0.0, 1.0)
     yq = torch.empty((bq, s, s), device="cuda")
+    api.qk_softmax(q, k, yq, d ** -0.5)
+    ref6 = torch.softmax((q[bq - 1, ::16].double() @ k[bq - 1].double().T) * d ** -0.5, dim=1)
+    g6 = parity_gate(torch, "softmax(Q K^T / sqrt(d)) (batch 255, every 16th row)",
+                     yq[bq - 1, ::16], ref6, rel_bound=2.0 ** -16, abs_floor=2.0 ** -14)
+    del ref6
     sec = time_device(torch, lambda: api.qk_softmax(q, k, yq, d ** -0.5), warm, steps, dist, world)
     alg = 2 * bq * s * d * 2 + bq * s * s * 4
     rec("qk_softmax", sec, alg, "GB/s", "hbm", peaks["hbm_gbs"], 1,
-        {"tflops": 2.0 * bq * s * s * d / sec / 1e12})
+        {"tflops": 2.0 * bq * s * s * d / sec / 1e12, "parity": g6})
     del q, k, yq
     torch.cuda.empty_cache()
     return out

@@ -23,10 +23,13 @@
 //                max / sum of exp2(scale*log2e*s), handed to group B through a
 //                double-buffered statistics slot;
 //   warps 6-17   group B (pass 2), three warps per lane quarter sharing each
-//                chunk's four 32-column groups round-robin: recompute,
-//                exp2(s*c - (m + log2 l)), transpose through an XOR-swizzled
-//                shared-memory tile so every global store is a full 128-byte
-//                row segment.
+//                chunk's four 32-row groups round-robin: recompute,
+//                exp2(s*c - (m + log2 l)). Pass 2's MMA swaps its operands
+//                (K chunk as A, Q band as B), so its accumulator holds the
+//                scores transposed: TMEM lane = key, column = score row. A
+//                warp's 32 lanes then hold 32 consecutive keys of one row, and
+//                each store instruction writes a full 128-byte row segment
+//                straight from registers, with no shared-memory transpose.
 // Every mbarrier wait is bounded (2 s); on a timeout the CTA raises the
 // device status word, drains its copies, frees TMEM and returns.
 // Other shapes use the two-step form (tcgen05 GEMM with the scale folded into
@@ -57,14 +60,12 @@ constexpr uint32_t kQBox = kRows * 64 * 2;   // 16 KB (one d-half)
 constexpr int kAWarps = 4;                   // pass 1: one warp per lane quarter
 constexpr int kBWarps = 12;                  // pass 2: three warps per lane quarter
 constexpr int kThreads = 64 + (kAWarps + kBWarps) * 32;  // 576
-constexpr uint32_t kStageTile = 32 * 32 * 4;         // [32 rows x 32 cols] f32
 constexpr uint64_t kLimitNs = 2000000000ull;
 
 struct QkSmem {
     uint8_t k[kKStages][kKBox];              // 80 KB
     uint8_t q[kQSlots][2][kQBox];            // 96 KB
-    uint8_t out[kBWarps][kStageTile];        // 48 KB (group B staging)
-    float2 stats[2][kRows];                  // [slot][row] = (max, sum)
+    alignas(16) float nmi[2][kRows];         // [slot][row] = -(max + log2 sum)
     uint64_t kfull[kKStages], kempty[kKStages];
     uint64_t qfull[kQSlots], qempty[kQSlots];
     uint64_t afull[2], aempty[2], bfull[2], bempty[2];
@@ -217,8 +218,9 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
         // ---------------- MMA issuer ----------------
         constexpr uint32_t kIdesc = tc::idesc_f16_f32(kRows, kChunk, 0, 0);
         uint32_t kit = 0, ait = 0, bit = 0;
-        // One accumulator chunk: Q slot x K chunk -> TMEM columns `dst`.
-        auto mma_chunk = [&](int qslot, uint32_t dst) -> bool {
+        // One accumulator chunk: Q slot x K chunk -> TMEM columns `dst`; with
+        // `keys_as_rows` the operands swap and the chunk lands transposed.
+        auto mma_chunk = [&](int qslot, uint32_t dst, bool keys_as_rows) -> bool {
             for (int h = 0; h < dh; ++h, ++kit) {
                 const int st = static_cast<int>(kit % kKStages);
                 if (!tc::mbar_wait(&sm.kfull[st], (kit / kKStages) & 1u, abort, kLimitNs)) {
@@ -229,8 +231,9 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                 const uint32_t k0 = tc::smem_u32(sm.k[st]);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    tc::mma_f16(dst, tc::smem_desc_sw128(q0 + kk * 32, 16, 1024),
-                                tc::smem_desc_sw128(k0 + kk * 32, 16, 1024), kIdesc,
+                    const uint64_t dq = tc::smem_desc_sw128(q0 + kk * 32, 16, 1024);
+                    const uint64_t dk = tc::smem_desc_sw128(k0 + kk * 32, 16, 1024);
+                    tc::mma_f16(dst, keys_as_rows ? dk : dq, keys_as_rows ? dq : dk, kIdesc,
                                 (h > 0 || kk > 0) ? 1u : 0u);
                 }
                 tc::mma_commit(&sm.kempty[st]);
@@ -238,7 +241,8 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
             return true;
         };
         // Both passes of a chunk from one K stage: pass 2 of unit step-1 into
-        // `db` (Q slot qb) and pass 1 of unit step into `da` (Q slot qa).
+        // `db` (Q slot qb, transposed) and pass 1 of unit step into `da` (Q
+        // slot qa).
         auto mma_chunk2 = [&](int qb, uint32_t db, int qa, uint32_t da) -> bool {
             for (int h = 0; h < dh; ++h, ++kit) {
                 const int st = static_cast<int>(kit % kKStages);
@@ -251,8 +255,8 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                 const uint32_t qa0 = tc::smem_u32(sm.q[qa][h]);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    tc::mma_f16(db, tc::smem_desc_sw128(qb0 + kk * 32, 16, 1024),
-                                tc::smem_desc_sw128(k0 + kk * 32, 16, 1024), kIdesc,
+                    tc::mma_f16(db, tc::smem_desc_sw128(k0 + kk * 32, 16, 1024),
+                                tc::smem_desc_sw128(qb0 + kk * 32, 16, 1024), kIdesc,
                                 (h > 0 || kk > 0) ? 1u : 0u);
                 }
 #pragma unroll
@@ -294,7 +298,7 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                     const uint32_t acc = bit & 1u;
                     ok = tc::mbar_wait(&sm.bempty[acc], ((bit >> 1) & 1u) ^ 1u, abort, kLimitNs);
                     tc::tc_fence_after();
-                    ok = ok && mma_chunk((step - 1) % kQSlots, tmem + 256 + acc * kChunk);
+                    ok = ok && mma_chunk((step - 1) % kQSlots, tmem + 256 + acc * kChunk, true);
                     if (ok) tc::mma_commit(&sm.bfull[acc]);
                     ++bit;
                 }
@@ -302,7 +306,7 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                     const uint32_t acc = ait & 1u;
                     ok = tc::mbar_wait(&sm.aempty[acc], ((ait >> 1) & 1u) ^ 1u, abort, kLimitNs);
                     tc::tc_fence_after();
-                    ok = ok && mma_chunk(step % kQSlots, tmem + acc * kChunk);
+                    ok = ok && mma_chunk(step % kQSlots, tmem + acc * kChunk, false);
                     if (ok) tc::mma_commit(&sm.afull[acc]);
                     ++ait;
                 }
@@ -358,14 +362,15 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                     m = mn;
                 }
             }
-            // hand (max, sum) of the row to group B
+            // hand -(m + log2 l) of the row to group B: y = exp2(s*c2 - m) / l
             {
                 const int slot = i & 1;
                 if (i >= 2 &&
                     !tc::mbar_wait(&sm.sempty[slot], ((i >> 1) - 1) & 1, abort, kLimitNs)) {
                     goto a_done;
                 }
-                sm.stats[slot][row] = make_float2(m, l);
+                // +inf score: the reference's exp(inf - inf) poisons the row
+                sm.nmi[slot][row] = (m == INFINITY) ? __int_as_float(0x7fffffff) : -(m + log2f(l));
                 warp_arrive(&sm.sfull[slot], lane);
             }
         }
@@ -373,70 +378,51 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
     } else if (warp >= 2 + kAWarps) {
         // ---------------- group B: pass 2 (normalised write) ----------------
         const int ew = warp - 2 - kAWarps;
-        const int quarter = warp & 3;
-        const int sub = ew >> 2;  // 0..2: which of the quarter's three warps
-        const int row = quarter * 32 + lane;
+        const int quarter = warp & 3;  // TMEM lanes = the chunk's keys quarter*32 + lane
+        const int sub = ew >> 2;       // 0..2: which of the quarter's three warps
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-        uint8_t* const tile = sm.out[ew];
-        const int jj = lane & 7;
         uint32_t bit = 0;
         for (int i = 0; i < n; ++i) {
             const int u = unit_of(i);
             const int b = u / bands, band = u - b * bands;
-            float mi;  // m + log2(l): y = exp2(s * c2 - mi) = exp2(s * c2 - m) / l
-            {
-                const int slot = i & 1;
-                if (!tc::mbar_wait(&sm.sfull[slot], (i >> 1) & 1, abort, kLimitNs)) goto b_done;
-                const float2 st = sm.stats[slot][row];
-                warp_arrive(&sm.sempty[slot], lane);
-                const float m = st.x, l = st.y;
-                // +inf score: the reference's exp(inf - inf) poisons the row
-                mi = (m == INFINITY) ? __int_as_float(0x7fffffff) : m + log2f(l);
-            }
+            const int slot = i & 1;
+            if (!tc::mbar_wait(&sm.sfull[slot], (i >> 1) & 1, abort, kLimitNs)) goto b_done;
+            const float* const nmi = sm.nmi[slot];
             float* const yband =
-                y + (static_cast<int64_t>(b) * s + band * kRows + quarter * 32) * s;
+                y + (static_cast<int64_t>(b) * s + band * kRows) * s + quarter * 32 + lane;
             for (int c = 0; c < chunks; ++c, ++bit) {
                 const uint32_t acc = bit & 1u;
                 if (!tc::mbar_wait(&sm.bfull[acc], (bit >> 1) & 1u, abort, kLimitNs)) goto b_done;
                 tc::tc_fence_after();
-                // The chunk's four 32-column groups, numbered 4*bit + g over the
+                // The chunk's four 32-row groups, numbered 4*bit + g over the
                 // whole run, are dealt round-robin to the quarter's three warps:
                 // this warp takes one or two of them.
                 const int g0 = (sub - static_cast<int>((4u * bit) % 3u) + 3) % 3;  // first g of ours
                 const int g1 = g0 + 3;                                          // second, if < 4
-                float* const ydst0 = yband + c * kChunk;
-                // One 32-column group: exponentials, swizzled staging, transposed
-                // stores (8 lanes per row, 4 rows per instruction, every store a
-                // full 128-byte row segment).
+                // One 32-row group: register j holds row g*32 + j at this lane's
+                // key, so every store is one row's 32 consecutive keys (128 B).
                 auto write_group = [&](const uint32_t (&r)[32], int g) {
+                    float* p = yband + c * kChunk + static_cast<int64_t>(g * 32) * s;
+                    const float4* const nm = reinterpret_cast<const float4*>(nmi + g * 32);
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
+                        const float4 v = nm[j];  // same address in every lane
                         // exponent arguments two at a time (packed f32x2 FMA)
                         const float2 t0 = __ffma2_rn(
                             make_float2(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1])),
-                            make_float2(c2, c2), make_float2(-mi, -mi));
+                            make_float2(c2, c2), make_float2(v.x, v.y));
                         const float2 t1 = __ffma2_rn(
                             make_float2(__uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])),
-                            make_float2(c2, c2), make_float2(-mi, -mi));
-                        float4 v;
-                        v.x = ex2(t0.x);
-                        v.y = ex2(t0.y);
-                        v.z = ex2(t1.x);
-                        v.w = ex2(t1.y);
-                        // row `lane`, 16-byte chunk j, XOR-swizzled (conflict-free)
-                        *reinterpret_cast<float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4)) = v;
+                            make_float2(c2, c2), make_float2(v.z, v.w));
+                        __stcs(p, ex2(t0.x));
+                        p += s;
+                        __stcs(p, ex2(t0.y));
+                        p += s;
+                        __stcs(p, ex2(t1.x));
+                        p += s;
+                        __stcs(p, ex2(t1.y));
+                        p += s;
                     }
-                    __syncwarp();
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) {
-                        const int rr = t * 4 + (lane >> 3);
-                        const float4 v = *reinterpret_cast<const float4*>(
-                            tile + rr * 128 + ((jj ^ (rr & 7)) << 4));
-                        __stcs(reinterpret_cast<float4*>(ydst0 + static_cast<int64_t>(rr) * s +
-                                                         g * 32) + jj,
-                               v);
-                    }
-                    __syncwarp();
                 };
                 const uint32_t col = lane_addr + 256 + acc * kChunk;
                 uint32_t r0[32], r1[32];
@@ -449,6 +435,7 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                 write_group(r0, g0);
                 if (g1 < 4) write_group(r1, g1);
             }
+            warp_arrive(&sm.sempty[slot], lane);  // done with this unit's statistics
         }
     b_done:;
     }

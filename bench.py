@@ -264,10 +264,16 @@ def parity_gate(torch, name, got, ref64, ulp_bound=None, rel_bound=None, abs_flo
     return {"check": f"{name}: rel err <= {rel_bound}", "worst_rel": err, "pass": err <= rel_bound}
 
 
-def time_device(torch, fn, warmup, steps, dist, world, min_warm_s=0.0):
+def time_device(torch, fn, warmup, steps, dist, world, min_warm_s=0.0, stats=None):
     """W untimed steps (continued until min_warm_s has passed, so clock samples
     see the same steady load), then K steps between barrier+sync; CUDA events
-    on the current stream; max over ranks. Returns seconds per step."""
+    on the current stream; max over ranks. Returns seconds per step.
+
+    With a `stats` dict, K more steps follow, each bracketed by its own pair
+    of events, and `stats` receives this rank's median / min / max step time
+    (the reference's reporting: median of reps with min and max). That pass
+    is separate because events between steps would break the back-to-back
+    launch overlap the timed region measures."""
     t0 = time.perf_counter()
     done = 0
     while done < warmup or time.perf_counter() - t0 < min_warm_s:
@@ -292,6 +298,18 @@ def time_device(torch, fn, warmup, steps, dist, world, min_warm_s=0.0):
         t = torch.tensor([ms], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    if stats is not None:
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        for e0, e1 in ev:
+            e0.record()
+            fn()
+            e1.record()
+        torch.cuda.synchronize()
+        each = sorted(e0.elapsed_time(e1) for e0, e1 in ev)
+        stats.update({"median_ms": statistics.median(each), "min_ms": each[0],
+                      "max_ms": each[-1], "reps": steps,
+                      "how": "separate pass, one event pair per step (this rank)"})
     return ms / 1e3
 
 
@@ -352,9 +370,10 @@ def main():
             "dy": parity_gate(torch, "cos(x^2+3x)(2x+3)", dy[::4096],
                               torch.cos(us_) * (2.0 * xs_ + 3.0), ulp_bound=2)}
     del xs_, us_
+    step_ms = {}
     with ClockSampler(local) as clk:
         sec = time_device(torch, step, args.warmup, args.steps, dist, world,
-                          min_warm_s=args.min_warm_s)
+                          min_warm_s=args.min_warm_s, stats=step_ms)
     clocks = clk.summary()
     alg_bytes = n * BYTES_PER_ELEM_MAP2
     achieved = alg_bytes / sec / 1e9
@@ -450,7 +469,7 @@ def main():
             "roofline": roofline, "parity": gate, "cpu_baseline": cpu, "e2e": e2e,
             "gather": gather,
             "gpu_launches": args.steps + sum(c.get("gpu_launches", 0) for c in configs.values()),
-            "clocks": clocks, "configs": configs, "library": mb.version(),
+            "clocks": clocks, "step_ms": step_ms, "configs": configs, "library": mb.version(),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -502,6 +521,7 @@ def run_case(args):
 def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     out = {}
     steps, warm = args.steps, args.warmup
+    last = {}  # per-step median / min / max of the most recent time_device call
 
     def rec(name, sec, work, unit, bound, peak, launches, extra=None):
         achieved = work / sec / (1e9 if unit == "GB/s" else 1e12)
@@ -509,7 +529,8 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
              "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                           "frac": achieved / peak,
                           "traffic": traffic.get(name, {}).get("bytes_per_launch")},
-             "gpu_launches": launches * steps}
+             "gpu_launches": launches * steps, "step_ms": dict(last)}
+        last.clear()
         if extra:
             d.update(extra)
         out[name] = d
@@ -532,7 +553,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     x64 = xs1[0][::1024].double()
     g1 = parity_gate(torch, "sin(x^2+3x)", ys1[0][::1024], torch.sin(x64 * x64 + 3.0 * x64),
                      ulp_bound=2)
-    sec = time_device(torch, step1, warm, steps, dist, world)
+    sec = time_device(torch, step1, warm, steps, dist, world, stats=last)
     rec("map1", sec, n1 * 8, "GB/s", "hbm", peaks["hbm_gbs"], 1,
         {"note": "steps rotate over 8 input/output pairs (1 GiB > L2), no flush",
          "parity": g1})
@@ -545,7 +566,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     api.softmax(xs, ys)
     g3 = parity_gate(torch, "softmax rows", ys[::1024],
                      torch.softmax(xs[::1024].double(), dim=1), ulp_bound=2)
-    sec = time_device(torch, lambda: api.softmax(xs, ys), warm, steps, dist, world)
+    sec = time_device(torch, lambda: api.softmax(xs, ys), warm, steps, dist, world, stats=last)
     rec("softmax", sec, 2 * 4 * 65536 * 4096, "GB/s", "hbm", peaks["hbm_gbs"], 1,
         {"parity": g3})
     del xs, ys
@@ -565,7 +586,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     g4 = {"check": "f16 GEMM: |C - C_f64| <= 2^-12 sum|a b| (every 128th row)",
           "worst": err4, "pass": err4 <= 2.0 ** -12}
     del ref4, mag4
-    sec = time_device(torch, lambda: api.gemm(a, b, c), warm, steps, dist, world)
+    sec = time_device(torch, lambda: api.gemm(a, b, c), warm, steps, dist, world, stats=last)
     rec("gemm_f16", sec, 2.0 * n4 ** 3, "TFLOP/s", "tensor", peaks["bf16_tflops"], 1,
         {"peak_note": "peak = measured cuBLAS bf16 dense burst (f16 has the same rate)",
          "parity": g4})
@@ -580,7 +601,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
             (a.double().abs() @ b.double().abs())).max().item()
     g5 = {"check": "f32 GEMM: |C - C_f64| <= 2^-14 sum|a b|", "worst": err5,
           "pass": err5 <= 2.0 ** -14}
-    sec = time_device(torch, lambda: api.gemm(a, b, c), warm, steps, dist, world)
+    sec = time_device(torch, lambda: api.gemm(a, b, c), warm, steps, dist, world, stats=last)
     rec("gemm_f32_1024", sec, 2.0 * 1024 ** 3, "TFLOP/s", "fp32-simt", 80.0, 1,
         {"peak_note": "nominal FP32 SIMT 80 TFLOP/s (context only)", "parity": g5})
     del a, b, c
@@ -597,7 +618,8 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     g6 = parity_gate(torch, "softmax(Q K^T / sqrt(d)) (batch 255, every 16th row)",
                      yq[bq - 1, ::16], ref6, rel_bound=2.0 ** -16, abs_floor=2.0 ** -14)
     del ref6
-    sec = time_device(torch, lambda: api.qk_softmax(q, k, yq, d ** -0.5), warm, steps, dist, world)
+    sec = time_device(torch, lambda: api.qk_softmax(q, k, yq, d ** -0.5), warm, steps, dist, world,
+                      stats=last)
     alg = 2 * bq * s * d * 2 + bq * s * s * 4
     rec("qk_softmax", sec, alg, "GB/s", "hbm", peaks["hbm_gbs"], 1,
         {"tflops": 2.0 * bq * s * s * d / sec / 1e12, "parity": g6})

@@ -521,7 +521,18 @@ def run_case(args):
 def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     out = {}
     steps, warm = args.steps, args.warmup
-    last = {}  # per-step median / min / max of the most recent time_device call
+    last = {}  # per-step statistics and the sustained time of the latest measure()
+
+    def measure(fn):
+        """Seconds per step of a burst: each config starts from an idle GPU (1 s
+        pause), so its number does not depend on the heat the previous config
+        left under the 1 kW power limit; then the same steps once more after
+        1.5 s of continuous running, reported beside it as `sustained`."""
+        time.sleep(1.0)
+        sec = time_device(torch, fn, warm, steps, dist, world, stats=last)
+        sus = time_device(torch, fn, 0, steps, dist, world, min_warm_s=1.5)
+        last["sustained_ms_per_step"] = sus * 1e3
+        return sec
 
     def rec(name, sec, work, unit, bound, peak, launches, extra=None):
         achieved = work / sec / (1e9 if unit == "GB/s" else 1e12)
@@ -529,7 +540,16 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
              "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                           "frac": achieved / peak,
                           "traffic": traffic.get(name, {}).get("bytes_per_launch")},
-             "gpu_launches": launches * steps, "step_ms": dict(last)}
+             "gpu_launches": launches * steps}
+        sus = last.pop("sustained_ms_per_step", None)
+        d["step_ms"] = dict(last)
+        if sus is not None:
+            per_gpu = work / (sus / 1e3) / (1e9 if unit == "GB/s" else 1e12)
+            # a long-running GEMM is judged against the measured sustained cuBLAS rate
+            sus_peak = (peaks.get("bf16_tflops_sustained") or peak) if bound == "tensor" else peak
+            d["sustained"] = {"ms_per_step": sus, "value": world * per_gpu, "peak": sus_peak,
+                              "frac": per_gpu / sus_peak,
+                              "note": "same steps after 1.5 s of continuous running"}
         last.clear()
         if extra:
             d.update(extra)
@@ -553,7 +573,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     x64 = xs1[0][::1024].double()
     g1 = parity_gate(torch, "sin(x^2+3x)", ys1[0][::1024], torch.sin(x64 * x64 + 3.0 * x64),
                      ulp_bound=2)
-    sec = time_device(torch, step1, warm, steps, dist, world, stats=last)
+    sec = measure(step1)
     rec("map1", sec, n1 * 8, "GB/s", "hbm", peaks["hbm_gbs"], 1,
         {"note": "steps rotate over 8 input/output pairs (1 GiB > L2), no flush",
          "parity": g1})
@@ -566,7 +586,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     api.softmax(xs, ys)
     g3 = parity_gate(torch, "softmax rows", ys[::1024],
                      torch.softmax(xs[::1024].double(), dim=1), ulp_bound=2)
-    sec = time_device(torch, lambda: api.softmax(xs, ys), warm, steps, dist, world, stats=last)
+    sec = measure(lambda: api.softmax(xs, ys))
     rec("softmax", sec, 2 * 4 * 65536 * 4096, "GB/s", "hbm", peaks["hbm_gbs"], 1,
         {"parity": g3})
     del xs, ys
@@ -586,7 +606,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     g4 = {"check": "f16 GEMM: |C - C_f64| <= 2^-12 sum|a b| (every 128th row)",
           "worst": err4, "pass": err4 <= 2.0 ** -12}
     del ref4, mag4
-    sec = time_device(torch, lambda: api.gemm(a, b, c), warm, steps, dist, world, stats=last)
+    sec = measure(lambda: api.gemm(a, b, c))
     rec("gemm_f16", sec, 2.0 * n4 ** 3, "TFLOP/s", "tensor", peaks["bf16_tflops"], 1,
         {"peak_note": "peak = measured cuBLAS bf16 dense burst (f16 has the same rate)",
          "parity": g4})
@@ -601,7 +621,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
             (a.double().abs() @ b.double().abs())).max().item()
     g5 = {"check": "f32 GEMM: |C - C_f64| <= 2^-14 sum|a b|", "worst": err5,
           "pass": err5 <= 2.0 ** -14}
-    sec = time_device(torch, lambda: api.gemm(a, b, c), warm, steps, dist, world, stats=last)
+    sec = measure(lambda: api.gemm(a, b, c))
     rec("gemm_f32_1024", sec, 2.0 * 1024 ** 3, "TFLOP/s", "fp32-simt", 80.0, 1,
         {"peak_note": "nominal FP32 SIMT 80 TFLOP/s (context only)", "parity": g5})
     del a, b, c
@@ -618,8 +638,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     g6 = parity_gate(torch, "softmax(Q K^T / sqrt(d)) (batch 255, every 16th row)",
                      yq[bq - 1, ::16], ref6, rel_bound=2.0 ** -16, abs_floor=2.0 ** -14)
     del ref6
-    sec = time_device(torch, lambda: api.qk_softmax(q, k, yq, d ** -0.5), warm, steps, dist, world,
-                      stats=last)
+    sec = measure(lambda: api.qk_softmax(q, k, yq, d ** -0.5))
     alg = 2 * bq * s * d * 2 + bq * s * s * 4
     rec("qk_softmax", sec, alg, "GB/s", "hbm", peaks["hbm_gbs"], 1,
         {"tflops": 2.0 * bq * s * s * d / sec / 1e12, "parity": g6})

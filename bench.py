@@ -321,7 +321,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--headline-only", action="store_true")
     ap.add_argument("--min-warm-s", type=float, default=1.5,
-                    help="headline warm-up continues at least this long (clock samples)")
+                    help="headline warm-up continues at least this long (clock samples); "
+                         "also the run-in of each config's sustained figure (0: none)")
     ap.add_argument("--case", default=None,
                     choices=["map1", "map2", "softmax", "gemm", "gemm_f32", "qk"],
                     help="run one kernel W+K times (profiling target), no JSON line")
@@ -527,11 +528,13 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
         """Seconds per step of a burst: each config starts from an idle GPU (1 s
         pause), so its number does not depend on the heat the previous config
         left under the 1 kW power limit; then the same steps once more after
-        1.5 s of continuous running, reported beside it as `sustained`."""
+        --min-warm-s (default 1.5 s) of continuous running, reported beside it
+        as `sustained` (skipped with --min-warm-s 0)."""
         time.sleep(1.0)
         sec = time_device(torch, fn, warm, steps, dist, world, stats=last)
-        sus = time_device(torch, fn, 0, steps, dist, world, min_warm_s=1.5)
-        last["sustained_ms_per_step"] = sus * 1e3
+        if args.min_warm_s > 0:
+            sus = time_device(torch, fn, 0, steps, dist, world, min_warm_s=args.min_warm_s)
+            last["sustained_ms_per_step"] = sus * 1e3
         return sec
 
     def rec(name, sec, work, unit, bound, peak, launches, extra=None):
@@ -549,7 +552,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
             sus_peak = (peaks.get("bf16_tflops_sustained") or peak) if bound == "tensor" else peak
             d["sustained"] = {"ms_per_step": sus, "value": world * per_gpu, "peak": sus_peak,
                               "frac": per_gpu / sus_peak,
-                              "note": "same steps after 1.5 s of continuous running"}
+                              "note": f"same steps after {args.min_warm_s} s of continuous running"}
         last.clear()
         if extra:
             d.update(extra)

@@ -55,12 +55,15 @@ __device__ __forceinline__ double blockSum(double v, double* sm) {
 // FMA with fl64(ln2/256): |k| <= 44320 keeps the constant's error below 1e-14
 // relative), |r| <= ln2/512, so 1 + r + r^2/2 has relative error < 4.2e-10
 // (under 0.01 f32 ulp); then 2^(k/256) = 2^(k>>8) * T[k&255] with the power
-// of two added to T's exponent field. d < -120 gives 0 (such terms are below
-// half the smallest f32 subnormal relative to any row sum >= 1 and add
-// nothing to it); NaN propagates; -inf gives 0. tab[j] = 2^(j/256).
+// of two added to T's exponent field. d < -700 (and -inf) is clamped to -700,
+// which still builds a normal scale (2^-1010): every term below -120 is under
+// half the smallest f32 subnormal relative to any row sum >= 1, so it adds
+// nothing to the sum and stores 0, as exp(d) would. NaN passes the clamp and
+// propagates. tab[j] = 2^(j/256).
 __device__ __forceinline__ double exp_neg_tab(double d, const double* tab) {
     // Branch-free: every lane evaluates the formula (the table index k & 255 is
-    // always in range), then out-of-range lanes take 0 or their NaN.
+    // always in range).
+    d = (d < -700.0) ? -700.0 : d;
     const double kMagic = 6755399441055744.0;  // 1.5 * 2^52
     const double t = fma(d, 369.3299304675746, kMagic);
     const double kd = t - kMagic;
@@ -71,8 +74,14 @@ __device__ __forceinline__ double exp_neg_tab(double d, const double* tab) {
     const double tj = tab[k & 255];
     const double scale = __hiloint2double(__double2hiint(tj) + ((k >> 8) << 20),
                                           __double2loint(tj));
-    const double e = p * scale;
-    return (d >= -120.0) ? e : ((d != d) ? d : 0.0);
+    return p * scale;
+}
+
+// max of three, NaN-ignoring like the reference's (x > r) ? x : r scan.
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
@@ -137,10 +146,8 @@ softmax_rows_tma(const float* __restrict__ x, float* __restrict__ y, int64_t row
             const int c = tid + j * kRowThreads;
             if (kFull || c < nvec) {
                 v[j] = xr[c];
-                m = (v[j].x > m) ? v[j].x : m;
-                m = (v[j].y > m) ? v[j].y : m;
-                m = (v[j].z > m) ? v[j].z : m;
-                m = (v[j].w > m) ? v[j].w : m;
+                m = max3(m, v[j].x, v[j].y);
+                m = max3(m, v[j].z, v[j].w);
             }
         }
         m = warpMax(m);

@@ -281,9 +281,12 @@ def time_device(torch, fn, warmup, steps, dist, world, min_warm_s=0.0, stats=Non
         done += 1
         if done % 16 == 0:
             torch.cuda.synchronize()
-    torch.cuda.synchronize()
+    # Barrier, then synchronize: the barrier's collective queues behind the
+    # last warm-up steps instead of leaving the GPU idle for its length right
+    # before the timed region.
     if world > 1:
         dist.barrier()
+    torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record()

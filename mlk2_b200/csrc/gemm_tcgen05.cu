@@ -24,6 +24,7 @@
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <climits>
 #include <mutex>
 
@@ -479,7 +480,7 @@ int launchGemmTc(const void* a, const void* b, float* c, int64_t batch, int64_t 
     } else {
         if (int st = makeTmapF16(&tb, b, k, n, kBK, 64)) return st;
     }
-    static bool attr[2][64] = {};
+    static std::atomic<bool> attr[2][64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr[b_kmajor][dev]) {
@@ -515,7 +516,7 @@ int launchGemmPair(const void* a, const void* b, float* c, int64_t m, int64_t n,
     CUtensorMap ta, tb;
     if (int st = makeTmapF16(&ta, a, m, k, kBM, kBK)) return st;
     if (int st = makeTmapF16(&tb, b, k, n, kBK, 64)) return st;
-    static bool attr[64] = {};
+    static std::atomic<bool> attr[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr[dev]) {

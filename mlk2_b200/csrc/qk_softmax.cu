@@ -37,6 +37,7 @@
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdio>
 
 #include "common.cuh"
@@ -475,7 +476,7 @@ extern "C" int mlkb_qk_softmax_f16(const void* q, const void* k, float* y, int64
     CUtensorMap tq, tk;
     if (int rc = makeTmapF16(&tq, q, batch * s, d, kRows, 64)) return rc;
     if (int rc = makeTmapF16(&tk, k, batch * s, d, kChunk, 64)) return rc;
-    static bool attr[64] = {false};
+    static std::atomic<bool> attr[64];
     int dev = 0;
     cudaGetDevice(&dev);
     int optin = 0;

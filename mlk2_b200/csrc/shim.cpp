@@ -50,7 +50,7 @@ int setCudaError(int code, cudaError_t e, const char* what) {
 int okStatus() { return MLKB_OK; }
 
 int smCount() {
-    static int cache[64] = {0};
+    static std::atomic<int> cache[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
     if (cache[dev] == 0) {

@@ -13,6 +13,8 @@
 // in f64, and y = e * (1/s) rounded once to f32: read once, write once.
 // Rows that do not fit the register tile (or are not float4-aligned) take a
 // three-pass streaming kernel with the same arithmetic.
+#include <atomic>
+
 #include "common.cuh"
 #include "tc_common.cuh"
 
@@ -320,7 +322,7 @@ template <int NV, bool kFull>
 int launchRowsTma(const float* x, float* y, int64_t rows, int64_t cols, cudaStream_t s) {
     const uint32_t buf = ((static_cast<uint32_t>(cols) * 4u + 127u) & ~127u);
     const size_t smem = 2 * static_cast<size_t>(buf);
-    static bool attr[64] = {false};
+    static std::atomic<bool> attr[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr[dev]) {

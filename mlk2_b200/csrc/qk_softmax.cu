@@ -30,6 +30,8 @@
 //                warp's 32 lanes then hold 32 consecutive keys of one row, and
 //                each store instruction writes a full 128-byte row segment
 //                straight from registers, with no shared-memory transpose.
+// The row length is a template constant for s = 1024, 2048 and 4096 (a
+// runtime value otherwise), so pass-2 stores use immediate row offsets.
 // Every mbarrier wait is bounded (2 s); on a timeout the CTA raises the
 // device status word, drains its copies, frees TMEM and returns.
 // Other shapes use the two-step form (tcgen05 GEMM with the scale folded into
@@ -96,10 +98,12 @@ __device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
     if (lane == 0) tc::mbar_arrive(bar);
 }
 
+template <int kS>
 __global__ void __launch_bounds__(kThreads, 1)
 qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k, float* __restrict__ y, int batch,
-                   int s, int d, float c2, int* __restrict__ status) {
+                   int s_in, int d, float c2, int* __restrict__ status) {
+    const int s = kS != 0 ? kS : s_in;  // row length, a constant where specialised
     // The kernel has no static shared memory, so the dynamic window starts at
     // the 1024-byte aligned base the 128B-swizzled tiles need.
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -403,7 +407,7 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                 // One 32-row group: register j holds row g*32 + j at this lane's
                 // key, so every store is one row's 32 consecutive keys (128 B).
                 auto write_group = [&](const uint32_t (&r)[32], int g) {
-                    float* p = yband + c * kChunk + static_cast<int64_t>(g * 32) * s;
+                    float* const p = yband + c * kChunk + static_cast<int64_t>(g * 32) * s;
                     const float4* const nm = reinterpret_cast<const float4*>(nmi + g * 32);
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
@@ -415,14 +419,10 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                         const float2 t1 = __ffma2_rn(
                             make_float2(__uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])),
                             make_float2(c2, c2), make_float2(v.z, v.w));
-                        __stcs(p, ex2(t0.x));
-                        p += s;
-                        __stcs(p, ex2(t0.y));
-                        p += s;
-                        __stcs(p, ex2(t1.x));
-                        p += s;
-                        __stcs(p, ex2(t1.y));
-                        p += s;
+                        __stcs(p + (4 * j + 0) * s, ex2(t0.x));
+                        __stcs(p + (4 * j + 1) * s, ex2(t0.y));
+                        __stcs(p + (4 * j + 2) * s, ex2(t1.x));
+                        __stcs(p + (4 * j + 3) * s, ex2(t1.y));
                     }
                 };
                 const uint32_t col = lane_addr + 256 + acc * kChunk;
@@ -476,7 +476,7 @@ extern "C" int mlkb_qk_softmax_f16(const void* q, const void* k, float* y, int64
     CUtensorMap tq, tk;
     if (int rc = makeTmapF16(&tq, q, batch * s, d, kRows, 64)) return rc;
     if (int rc = makeTmapF16(&tk, k, batch * s, d, kChunk, 64)) return rc;
-    static std::atomic<bool> attr[64];
+    static std::atomic<bool> attr[4][64];
     int dev = 0;
     cudaGetDevice(&dev);
     int optin = 0;
@@ -487,24 +487,32 @@ extern "C" int mlkb_qk_softmax_f16(const void* q, const void* k, float* y, int64
                  kSmemBytes, optin);
         return setError(MLKB_ERR_LAUNCH, msg);
     }
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
+    // Row lengths of 1024, 2048 and 4096 get a kernel specialised on them: a
+    // pass-2 warp then addresses all 32 rows of a group from one base by
+    // immediate offsets instead of stepping a 64-bit pointer per store.
+    const int which = s == 1024 ? 1 : s == 2048 ? 2 : s == 4096 ? 3 : 0;
+    decltype(&qk_softmax_tcgen05<0>) const kern =
+        which == 1 ? qk_softmax_tcgen05<1024>
+        : which == 2 ? qk_softmax_tcgen05<2048>
+        : which == 3 ? qk_softmax_tcgen05<4096>
+                     : qk_softmax_tcgen05<0>;
+    if (dev >= 0 && dev < 64 && !attr[which][dev]) {
         const cudaError_t e = cudaFuncSetAttribute(
-            qk_softmax_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize,
-            static_cast<int>(kSmemBytes));
+            kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
         if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "qk smem attribute");
-        attr[dev] = true;
+        attr[which][dev] = true;
     }
     const int64_t units = batch * (s / kRows);
     const int grid = static_cast<int>(units < smCount() ? units : smCount());
     // exp(scale * v) = exp2(scale * log2(e) * v)
     const float c2 = static_cast<float>(scale * 1.4426950408889634);
-    qk_softmax_tcgen05<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, y, static_cast<int>(batch),
-                                                          static_cast<int>(s), static_cast<int>(d),
-                                                          c2, deviceStatusPtr());
+    kern<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, y, static_cast<int>(batch),
+                                             static_cast<int>(s), static_cast<int>(d), c2,
+                                             deviceStatusPtr());
     const cudaError_t le = cudaGetLastError();
     if (le != cudaSuccess) {
         cudaFuncAttributes fa{};
-        cudaFuncGetAttributes(&fa, qk_softmax_tcgen05);
+        cudaFuncGetAttributes(&fa, kern);
         char msg[256];
         snprintf(msg, sizeof(msg),
                  "qk_softmax launch: %s (regs %d, max threads %d, static smem %zu, "

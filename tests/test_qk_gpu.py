@@ -32,11 +32,13 @@ def check(y, ref):
         float(np.max(np.abs(y - ref) / (ref + 2.0**-30)))
 
 
-# (2, 200, 64) and (1, 136, 96): s not a multiple of 128 or d not in {64, 128}
-# take the two-step form (single-CTA batched tcgen05 GEMM with K-major B and
-# the scale in its epilogue, then the row softmax in place).
-@pytest.mark.parametrize("shape", [(2, 256, 128), (3, 384, 64), (1, 2048, 128),
-                                   (2, 200, 64), (1, 136, 96)])
+# s = 1024, 2048 and 4096 run kernels specialised on the row length, other
+# multiples of 128 the runtime-length kernel. (2, 200, 64) and (1, 136, 96): s
+# not a multiple of 128 or d not in {64, 128} take the two-step form
+# (single-CTA batched tcgen05 GEMM with K-major B and the scale in its
+# epilogue, then the row softmax in place).
+@pytest.mark.parametrize("shape", [(2, 256, 128), (3, 384, 64), (2, 1024, 64), (1, 2048, 128),
+                                   (1, 4096, 128), (2, 200, 64), (1, 136, 96)])
 def test_qk_softmax(cuda, shape):
     batch, s, d = shape
     rng = np.random.default_rng(s + d)

@@ -449,21 +449,28 @@ PFN_cuTensorMapEncodeTiled_v12000 encodeFn() {
 
 }  // namespace
 
-// 2-D f16 tensor map over a row-major [rows, cols] matrix, box [box_rows, box_cols],
-// 128-byte swizzle (box_cols * 2 must be 128).
-int makeTmapF16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
-                int box_cols) {
+// 2-D tensor map over a row-major [rows, cols] matrix of `elem_bytes`-wide
+// elements, box [box_rows, box_cols]; out-of-range elements load as zero.
+int makeTmap2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, const void* base,
+               int64_t rows, int64_t cols, int box_rows, int box_cols,
+               CUtensorMapSwizzle swizzle) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = encodeFn();
     if (enc == nullptr) return setError(MLKB_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * elem_bytes};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
-                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = enc(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? okStatus() : setError(MLKB_ERR_INVALID, "tensor map encode failed");
+}
+
+// 2-D f16 tensor map, 128-byte swizzle (box_cols * 2 must be 128).
+int makeTmapF16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
+                int box_cols) {
+    return makeTmap2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, rows, cols, box_rows,
+                      box_cols, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 }  // namespace mlkb

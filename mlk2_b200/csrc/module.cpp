@@ -357,7 +357,8 @@ int classify(Module& m) {
             m.m = ba.dims[0];
             m.k = ba.dims[1];
             m.n = bb.dims[1];
-            if (bb.dims[0] != m.k || bo.dims[0] != m.m || bo.dims[1] != m.n) {
+            if (bb.dims[0] != m.k || bo.dims[0] != m.m || bo.dims[1] != m.n || m.m <= 0 ||
+                m.k <= 0 || m.n <= 0) {
                 return setError(MLKB_ERR_INVALID, "matmul operand shapes incompatible");
             }
             m.kind = MLKB_KIND_MATMUL;
@@ -409,7 +410,8 @@ int classify(Module& m) {
             const KBuffer& bq = m.buffers[mm.a];
             const KBuffer& bk = m.buffers[mm.b];
             if ((aConst || bConst) && bq.dims.size() == 2 && bk.dims.size() == 2 &&
-                bk.dims[0] == bq.dims[1]) {
+                bk.dims[0] == bq.dims[1] && bq.dims[0] > 0 && bq.dims[1] > 0 &&
+                bk.dims[1] > 0) {
                 m.scale = aConst ? e.a_value : e.b_value;
                 m.callA = static_cast<int>(mm.a);
                 m.callB = static_cast<int>(mm.b);
@@ -454,6 +456,19 @@ int parseModule(const char* json, Module& out) {
         kb.elements = getInt(b, "elements", -1);
         if (const JVal* d = b.get("dims"); d != nullptr && d->t == JVal::Arr) {
             for (const JVal& x : d->arr) kb.dims.push_back(x.i);
+        }
+        // Every later size computation starts from these shapes: each extent
+        // in [0, 2^31) and at most 2^40 elements, so byte counts cannot overflow.
+        constexpr int64_t kMaxElements = int64_t(1) << 40;
+        int64_t count = 1;
+        for (const int64_t d : kb.dims) {
+            if (d < 0 || d > INT32_MAX || (d != 0 && count > kMaxElements / d)) {
+                return setError(MLKB_ERR_INVALID, "module: buffer shape out of range");
+            }
+            count *= d;
+        }
+        if (kb.elements > kMaxElements) {
+            return setError(MLKB_ERR_INVALID, "module: buffer element count out of range");
         }
         m.buffers.push_back(std::move(kb));
     }

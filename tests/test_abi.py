@@ -130,6 +130,27 @@ def test_rejections():
     assert _status_of_create(kir.dumps(mm)) == mb.ERR_INVALID
 
 
+def test_shape_limits():
+    # empty or negative GEMM extents, an extent past 2^31 and a buffer past
+    # 2^40 elements are rejected before any size is computed from them
+    for m, k, n in [(0, 5, 6), (4, 0, 6), (4, 5, 0), (-4, 5, 6)]:
+        mm = kir.call_module("matmul", 4, 5, 6)
+        mm["buffers"][0]["dims"] = [m, k]
+        mm["buffers"][1]["dims"] = [k, n]
+        mm["buffers"][2]["dims"] = [m, n]
+        assert _status_of_create(kir.dumps(mm)) == mb.ERR_INVALID, (m, k, n)
+    big = kir.call_module("softmax", 4, 5)
+    big["buffers"][0]["dims"] = [2**31, 5]
+    assert _status_of_create(kir.dumps(big)) == mb.ERR_INVALID
+    huge = kir.call_module("matmul", 2**21, 2**21, 2**21)
+    assert _status_of_create(kir.dumps(huge)) == mb.ERR_INVALID   # 2^42 elements each
+    qk = kir.qk_softmax_module(256, 64, 0.125)
+    assert _status_of_create(kir.dumps(qk)) == mb.OK
+    qk["buffers"][0]["dims"] = [0, 64]
+    qk["buffers"][1]["dims"] = [64, 0]
+    assert _status_of_create(kir.dumps(qk)) != mb.OK
+
+
 def test_mlk_kernel_without_binding_reports_not_bound():
     L = mb.lib()
     assert L.mlk_bind_module(None) == 0

@@ -163,6 +163,14 @@ int mlkb_module_kind(const mlkb_module* module);
 /* Number of bindable (input + output) buffers, in table order. */
 int mlkb_module_num_buffers(const mlkb_module* module);
 
+/* Names of the kernels mlkb_module_run_dev launches for this module with
+ * these buffer dtypes, comma separated, into buf (cap bytes), e.g.
+ * "map_sin_dsin_f32" or "map_chain". Launches nothing. No reference
+ * counterpart: it reports which of this library's kernels a module reaches
+ * (the reference's emitter has one code path per module). */
+int mlkb_module_plan(const mlkb_module* module, const int32_t* dtypes, int32_t n_bufs,
+                     char* buf, int64_t cap);
+
 /*
  * Runs the module over DEVICE buffers on `device` / `stream`.
  *   bufs[i], dtypes[i]  buffer i of the module table (inputs then outputs),
@@ -184,8 +192,15 @@ int mlkb_module_run_dev(const mlkb_module* module, void* const* bufs,
  * copies outputs back, synchronously. n_gpus == 1 runs on the calling
  * thread's current device; n_gpus > 1 splits the work into contiguous
  * element / row shards over devices 0..n_gpus-1 (n_gpus <= 0: all visible
- * devices), one host thread and stream per device. Host buffers that are page-locked copy at full PCIe
- * speed; others are staged through pinned bounce buffers.
+ * devices), one host thread and stream per device. Copies go straight
+ * between the caller's buffers and the device: page-locked host buffers
+ * copy at full PCIe speed and overlap with compute, pageable ones are
+ * copied by the CUDA driver's own staging, without that overlap.
+ * Kinds: fused maps (element shards), Softmax / ReduceSum / MatMul (row
+ * shards, MatMul's B on every device) and the scaled-scores composite (row
+ * shards of Q, S, Sc and Y, Kt on every device). A module with nothing to
+ * run (every loop range empty) returns MLKB_OK; a kind this path cannot run
+ * returns MLKB_ERR_UNSUPPORTED, never MLKB_OK.
  */
 int mlkb_module_run_host(const mlkb_module* module, void* const* bufs,
                          const int32_t* dtypes, int32_t n_bufs, int64_t n,
@@ -209,7 +224,13 @@ int mlkb_map_sin_dsin_f32(const float* x, float* y, float* dy, int64_t n,
 /* Generic fused chain out[i] = chain(a[i], b[i], scalars) for any chain of
  * scalar-realisable ops (reference ExprEvaluator, kernel_buffers.cpp:106-178).
  * elem_dtype MLKB_F32 or MLKB_F64 for a, b and out alike; b may be NULL when
- * the chain never reads ElemB. At most 64 expressions and 64 scalars. */
+ * the chain never reads ElemB. At most 64 expressions (the reference's
+ * kMaxTempSlots); the scalar table may be any size, and a ScalarParam past
+ * its end reads 0 as in the reference (kernel_buffers.cpp:114-117).
+ * poly7_sin != 0 evaluates Sin with the reference's "poly7" family,
+ * families::polySin (compiler/include/mlk/support/math_families.h:81-90),
+ * bit-identical to it in f64; other ops keep the libm family
+ * (kernel_buffers.cpp:42-51). */
 int mlkb_map_chain(const mlkb_expr* exprs, int32_t n_exprs, int32_t poly7_sin,
                    const void* a, const void* b, void* out, int32_t elem_dtype,
                    int64_t n, const double* scalars, int64_t n_scalars,
@@ -248,6 +269,13 @@ int mlkb_gemm_f64(const double* a, const double* b, double* c, int64_t m,
  * :342-402, :290-340) fused into one kernel. */
 int mlkb_qk_softmax_f16(const void* q, const void* k, float* y, int64_t batch,
                         int64_t s, int64_t d, double scale, void* stream);
+
+/* The same composite with K given as the reference's MatMul B operand:
+ * Q f16 [batch, m, d], Kt f16 [batch, d, s] ([K, N] row-major per batch,
+ * reference kernel_buffers.cpp:1030-1036), Y f32 [batch, m, s]. Kt is read
+ * in place as the tensor cores' MN-major operand; nothing is transposed. */
+int mlkb_qk_softmax_kt_f16(const void* q, const void* kt, float* y, int64_t batch,
+                           int64_t m, int64_t s, int64_t d, double scale, void* stream);
 
 /* Deterministic synthetic inputs, generated on the device: a counter-based
  * SplitMix64 stream of (seed, stream_id, element index).

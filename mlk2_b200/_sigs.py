@@ -20,6 +20,7 @@ SIGNATURES = {
     "mlkb_module_destroy": (None, [vp]),
     "mlkb_module_kind": (i32, [vp]),
     "mlkb_module_num_buffers": (i32, [vp]),
+    "mlkb_module_plan": (i32, [vp, C.POINTER(i32), i32, C.c_char_p, i64]),
     "mlkb_module_run_dev": (i32, [vp, C.POINTER(vp), C.POINTER(i32), i32, i64, C.POINTER(f64), i64, i32, vp]),
     "mlkb_module_run_host": (i32, [vp, C.POINTER(vp), C.POINTER(i32), i32, i64, C.POINTER(f64), i64, i32]),
     "mlkb_map_sin_f32": (i32, [vp, vp, i64, vp]),
@@ -33,6 +34,7 @@ SIGNATURES = {
     "mlkb_gemm_f32": (i32, [vp, vp, vp, i64, i64, i64, i32, vp]),
     "mlkb_gemm_f64": (i32, [vp, vp, vp, i64, i64, i64, i32, vp]),
     "mlkb_qk_softmax_f16": (i32, [vp, vp, vp, i64, i64, i64, f64, vp]),
+    "mlkb_qk_softmax_kt_f16": (i32, [vp, vp, vp, i64, i64, i64, i64, f64, vp]),
     "mlkb_fill_f32": (i32, [vp, i64, u64, u32, i32, f64, f64, vp]),
     "mlkb_fill_f16": (i32, [vp, i64, u64, u32, i32, f64, f64, vp]),
 }

@@ -94,6 +94,15 @@ def qk_softmax(q, k, y, scale: float, stream=None):
                                     _stream(stream)))
 
 
+def qk_softmax_kt(q, kt, y, scale: float, stream=None):
+    """Y[b] = softmax_rows(scale * Q[b] @ Kt[b]): Q [batch, m, d], Kt [batch, d, s]."""
+    batch, m, d = q.shape
+    s = kt.shape[2]
+    assert tuple(kt.shape) == (batch, d, s) and tuple(y.shape) == (batch, m, s)
+    check(lib().mlkb_qk_softmax_kt_f16(_ptr(q), _ptr(kt), _ptr(y), batch, m, s, d, float(scale),
+                                       _stream(stream)))
+
+
 def fill(out, seed: int, stream_id: int, dist: str, lo: float, hi: float, stream=None):
     d = {"uniform": 0, "normal": 1}[dist]
     fn = lib().mlkb_fill_f32 if _dt_of(out) == F32 else lib().mlkb_fill_f16
@@ -136,6 +145,15 @@ class Module:
     @property
     def num_buffers(self) -> int:
         return lib().mlkb_module_num_buffers(self._h)
+
+    def plan(self, dtypes) -> str:
+        """Names of the kernels run_dev launches with these buffer dtypes
+        (MLKB_F16 / F32 / F64 codes, or arrays / tensors to take them from)."""
+        codes = [d if isinstance(d, int) else _dt_of(d) for d in dtypes]
+        arr = (C.c_int32 * len(codes))(*codes)
+        buf = C.create_string_buffer(512)
+        check(lib().mlkb_module_plan(self._h, arr, len(codes), buf, 512))
+        return buf.value.decode()
 
     def _args(self, bufs, scalars):
         n = len(bufs)

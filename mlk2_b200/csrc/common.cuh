@@ -27,6 +27,12 @@ int smCount();
 // mlkb_take_device_error() reads and clears it. nullptr if allocation failed.
 int* deviceStatusPtr();
 
+// Scaled-scores softmax Y[b] = softmax_rows(scale * Q[b] K[b]^T), Q [batch, m,
+// d] f16; K given as [batch, s, d] (kt false) or as Kt [batch, d, s] (kt
+// true); Y [batch, m, s] f32 (qk_softmax.cu).
+int launchQkSoftmax(const void* q, const void* k, float* y, int64_t batch, int64_t m, int64_t s,
+                    int64_t d, double scale, bool kt, cudaStream_t st);
+
 // Launch-check helper: maps a launch error to MLKB_ERR_LAUNCH.
 inline int checkLaunch(const char* what) {
     const cudaError_t e = cudaGetLastError();

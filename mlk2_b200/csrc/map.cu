@@ -261,24 +261,76 @@ struct DevExpr {
     double aval, bval;
 };
 
-constexpr int kMaxScalars = 64;
-
-// Passed by value as a __grid_constant__ kernel parameter (about 2 KB), so a
-// launch needs no device allocation.
+// Passed by value as a __grid_constant__ kernel parameter (about 1.6 KB), so
+// a launch needs no device allocation. ScalarParam operands are resolved on
+// the host into constants before launch (the reference reads scalars[idx],
+// or 0 past the table's end, kernel_buffers.cpp:114-117), so the table may
+// be any size.
 struct ChainParams {
     int32_t n_exprs;
     int32_t poly7;
-    int32_t n_scalars;
-    int32_t pad;
     DevExpr e[kMaxExprs];
-    double scalars[kMaxScalars];
 };
+
+// The reference's "poly7" sine family, families::polySin
+// (compiler/include/mlk/support/math_families.h:22-90): Cody-Waite reduction
+// by pi/2 = hi + lo, then a degree-13 odd sine or degree-12 even cosine
+// residual polynomial on [-pi/4, pi/4] picked by the quadrant. The reference
+// evaluates it in plain IEEE f64 without contraction; every step here is the
+// same correctly rounded operation in the same order (__d*_rn, no FMA), so
+// the result is bit-identical. The coefficients are the reference's own
+// published constants (math_families.h:30-35, :49-54).
+__device__ __forceinline__ double poly7_sin_reduced(double x) {
+    const double r2 = __dmul_rn(x, x);
+    double p = 1.58962301576546568060e-10;
+    p = __dadd_rn(__dmul_rn(p, r2), -2.50507477628578072866e-8);
+    p = __dadd_rn(__dmul_rn(p, r2), 2.75573136213857245213e-6);
+    p = __dadd_rn(__dmul_rn(p, r2), -1.98412698295895385996e-4);
+    p = __dadd_rn(__dmul_rn(p, r2), 8.33333333332211858878e-3);
+    p = __dadd_rn(__dmul_rn(p, r2), -1.66666666666666307295e-1);
+    return __dadd_rn(x, __dmul_rn(__dmul_rn(x, r2), p));  // x + x*r2*p, left to right
+}
+
+__device__ __forceinline__ double poly7_cos_reduced(double x) {
+    const double r2 = __dmul_rn(x, x);
+    double p = -1.13585365213876817300e-11;
+    p = __dadd_rn(__dmul_rn(p, r2), 2.08757530072652689750e-9);
+    p = __dadd_rn(__dmul_rn(p, r2), -2.75573142103085808917e-7);
+    p = __dadd_rn(__dmul_rn(p, r2), 2.48015872890001867312e-5);
+    p = __dadd_rn(__dmul_rn(p, r2), -1.38888888888783992457e-3);
+    p = __dadd_rn(__dmul_rn(p, r2), 4.16666666666666435770e-2);
+    // 1 - r2*0.5 + r2*r2*p, left to right
+    return __dadd_rn(__dsub_rn(1.0, __dmul_rn(r2, 0.5)), __dmul_rn(__dmul_rn(r2, r2), p));
+}
+
+__device__ __forceinline__ double poly7_sin(double x) {
+    const double kPio2Hi = 1.5707963267948965580e+00;  // also the reference's kPiHalf
+    const double kPio2Lo = 6.1232339957367660359e-17;
+    const double n = floor(__dadd_rn(__ddiv_rn(x, kPio2Hi), 0.5));
+    const double r = __dsub_rn(__dsub_rn(x, __dmul_rn(n, kPio2Hi)), __dmul_rn(n, kPio2Lo));
+    // For x NaN or infinite, fmod(n, 4) is NaN and r is NaN. The reference
+    // converts that NaN to int (INT_MIN on its x86-64 host) and its switch
+    // takes the default branch, -cos(r): the same branch here keeps even the
+    // NaN's sign bit-identical.
+    const double f = fmod(n, 4.0);
+    int q = (f == f) ? static_cast<int>(f) : 3;
+    if (q < 0) q += 4;
+    switch (q) {
+        case 0: return poly7_sin_reduced(r);
+        case 1: return poly7_cos_reduced(r);
+        case 2: return -poly7_sin_reduced(r);
+        default: return -poly7_cos_reduced(r);
+    }
+}
 
 // kF64Out: the chain result is stored in f64, so sin/cos use CUDA's double
 // routines (about 1 ULP of f64); f32 outputs use the fast reduction +
-// polynomial path above, whose error is far below f32 resolution.
+// polynomial path above, whose error is far below f32 resolution. With
+// `poly7` Sin is the reference's poly7 family in either case (Cos and the
+// other ops keep the libm family, as resolveFamily does,
+// kernel_buffers.cpp:42-51).
 template <bool kF64Out>
-__device__ __forceinline__ double apply(uint8_t op, double a, double b) {
+__device__ __forceinline__ double apply(uint8_t op, double a, double b, bool poly7) {
     switch (op) {
         case kAdd: return __dadd_rn(a, b);
         case kSub: return __dsub_rn(a, b);
@@ -288,7 +340,7 @@ __device__ __forceinline__ double apply(uint8_t op, double a, double b) {
         case kPow: return (a == 2.0 && b == 2.0) ? __dmul_rn(a, a) : ::pow(a, b);
         case kExp: return ::exp(a);
         case kLog: return a > 0.0 ? ::log(a) : 0.0;
-        case kSin: return kF64Out ? ::sin(a) : dev::sin_f64(a);
+        case kSin: return poly7 ? poly7_sin(a) : kF64Out ? ::sin(a) : dev::sin_f64(a);
         case kCos: {
             if (kF64Out) return ::cos(a);
             double s, c;
@@ -332,11 +384,10 @@ __global__ void chain_kernel(const __grid_constant__ ChainParams p,
                 if (kind == kConst) v = val;
                 else if (kind == kElemA) v = va;
                 else if (kind == kElemB) v = vb;
-                else if (kind == kScalar) v = (idx >= 0 && idx < p.n_scalars) ? p.scalars[idx] : 0.0;
                 else if (kind == kTemp) v = t[idx];  // 0 <= idx < k (host-checked)
                 x[s] = v;
             }
-            t[k] = apply<sizeof(T) == 8>(e.op, x[0], e.unary ? 0.0 : x[1]);
+            t[k] = apply<sizeof(T) == 8>(e.op, x[0], e.unary ? 0.0 : x[1], p.poly7 != 0);
         }
         out[i] = static_cast<T>(t[p.n_exprs - 1]);
     }
@@ -375,9 +426,6 @@ int checkChain(const mlkb_expr* exprs, int32_t n_exprs, bool has_b) {
             if (kind == kTemp && (idx < 0 || idx >= k)) {
                 return setError(MLKB_ERR_UNSUPPORTED, "chain: temp operand is not an earlier expression");
             }
-            if (kind == kScalar && (idx < -32768 || idx > 32767)) {
-                return setError(MLKB_ERR_INVALID, "chain: scalar index out of range");
-            }
         }
     }
     return okStatus();
@@ -406,25 +454,30 @@ extern "C" int mlkb_map_chain(const mlkb_expr* exprs, int32_t n_exprs, int32_t p
     if (elem_dtype != MLKB_F32 && elem_dtype != MLKB_F64) {
         return setError(MLKB_ERR_INVALID, "chain: element dtype must be f32 or f64");
     }
-    if (n_scalars < 0 || n_scalars > 64 || (n_scalars > 0 && scalars == nullptr)) {
-        return setError(MLKB_ERR_INVALID, "chain: 0..64 scalars required");
+    if (n_scalars < 0 || (n_scalars > 0 && scalars == nullptr)) {
+        return setError(MLKB_ERR_INVALID, "chain: bad scalar table");
     }
-    if (n == 0) return okStatus();
     ChainParams p{};
     p.n_exprs = n_exprs;
-    p.poly7 = poly7_sin;
+    p.poly7 = poly7_sin != 0 ? 1 : 0;
     for (int k = 0; k < n_exprs; ++k) {
-        p.e[k].op = static_cast<uint8_t>(exprs[k].op);
-        p.e[k].akind = static_cast<uint8_t>(exprs[k].a_kind);
-        p.e[k].bkind = static_cast<uint8_t>(exprs[k].b_kind);
-        p.e[k].unary = isUnaryOp(exprs[k].op) ? 1 : 0;
-        p.e[k].aidx = static_cast<int16_t>(exprs[k].a_index);
-        p.e[k].bidx = static_cast<int16_t>(exprs[k].b_index);
-        p.e[k].aval = exprs[k].a_value;
-        p.e[k].bval = exprs[k].b_value;
+        const mlkb_expr& x = exprs[k];
+        DevExpr& e = p.e[k];
+        e.op = static_cast<uint8_t>(x.op);
+        e.unary = isUnaryOp(x.op) ? 1 : 0;
+        for (int side = 0; side < 2; ++side) {
+            int kind = side == 0 ? x.a_kind : x.b_kind;
+            const int64_t idx = side == 0 ? x.a_index : x.b_index;
+            double val = side == 0 ? x.a_value : x.b_value;
+            if (kind == kScalar) {  // a ScalarParam is a constant for the whole launch
+                val = (idx >= 0 && idx < n_scalars) ? scalars[idx] : 0.0;
+                kind = kConst;
+            }
+            (side == 0 ? e.akind : e.bkind) = static_cast<uint8_t>(kind);
+            (side == 0 ? e.aidx : e.bidx) = static_cast<int16_t>(kind == kTemp ? idx : 0);
+            (side == 0 ? e.aval : e.bval) = val;
+        }
     }
-    p.n_scalars = static_cast<int32_t>(n_scalars);
-    for (int64_t k = 0; k < n_scalars; ++k) p.scalars[k] = scalars[k];
     cudaStream_t s = asStream(stream);
     const int grid = gridFor(n, 256);
     if (elem_dtype == MLKB_F32) {

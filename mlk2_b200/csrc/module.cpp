@@ -388,7 +388,9 @@ int classify(Module& m) {
         return okStatus();
     }
 
-    // Call(MatMul) -> Loop{ElemA * const} -> Call(Softmax) composite.
+    // Call(MatMul) -> Loop{ElemA * const} -> Call(Softmax) composite: the
+    // executor runs the three top-level nodes in order (:921-1085), so
+    // S (+)= Q*Kt, Sc[i] = S[i] * scale over the loop range, Y = softmax(Sc).
     if (tops.size() == 3 && m.nodes[tops[0]].op == KOp::Call &&
         m.nodes[tops[1]].op == KOp::Loop && m.nodes[tops[2]].op == KOp::Call) {
         const KNode& mm = m.nodes[tops[0]];
@@ -403,24 +405,59 @@ int classify(Module& m) {
         if (callMath(mm) == kMathMatMul && callMath(sm) == kMathSoftmax && comp != nullptr &&
             store != nullptr && comp->exprs.size() == 1 && comp->exprs[0].op == 2 &&
             validBuf(mm.a) && validBuf(mm.b) && validBuf(mm.out) && validBuf(sm.out) &&
-            comp->a == mm.out && store->out == sm.a) {
+            validBuf(store->out) && comp->a == mm.out && store->out == sm.a) {
             const mlkb_expr& e = comp->exprs[0];
             const bool aConst = e.a_kind == 0 && e.b_kind == 1;
             const bool bConst = e.b_kind == 0 && e.a_kind == 1;
             const KBuffer& bq = m.buffers[mm.a];
             const KBuffer& bk = m.buffers[mm.b];
-            if ((aConst || bConst) && bq.dims.size() == 2 && bk.dims.size() == 2 &&
-                bk.dims[0] == bq.dims[1] && bq.dims[0] > 0 && bq.dims[1] > 0 &&
-                bk.dims[1] > 0) {
+            const KBuffer& bs = m.buffers[mm.out];
+            const KBuffer& bsc = m.buffers[store->out];
+            const KBuffer& by = m.buffers[sm.out];
+            if ((aConst || bConst) && bq.dims.size() == 2 && bk.dims.size() == 2) {
+                const int64_t rows = bq.dims[0], d = bq.dims[1], keys = bk.dims[1];
+                auto is2 = [&](const KBuffer& b) {
+                    return b.dims.size() == 2 && b.dims[0] == rows && b.dims[1] == keys;
+                };
+                // The shape checks execGemm and execSoftmaxCall make (:1014-1037, :294-316).
+                if (bk.dims[0] != d || rows <= 0 || d <= 0 || keys <= 0 || !is2(bs) || !is2(by) ||
+                    (!bsc.dims.empty() && !is2(bsc))) {
+                    return setError(MLKB_ERR_INVALID, "qk composite: operand shapes incompatible");
+                }
+                if (mm.a == mm.out || mm.b == mm.out || store->out == sm.out || mm.out == sm.out ||
+                    !(bq.input && bk.input) || !by.output) {
+                    return setError(MLKB_ERR_UNSUPPORTED,
+                                    "qk composite: Q and Kt must be inputs and Y an output, "
+                                    "all distinct");
+                }
+                // The scores S and scaled scores Sc are either both temps
+                // (only Y observable: the fused kernel) or both outputs.
+                const bool sTemp = bs.temp && !bs.output, scTemp = bsc.temp && !bsc.output;
+                if (sTemp != scTemp || (!sTemp && !(bs.output && bsc.output))) {
+                    return setError(MLKB_ERR_UNSUPPORTED,
+                                    "qk composite: S and Sc must be both temps or both outputs");
+                }
+                if (loop.begin < 0 || (loop.end >= 0 && loop.end > rows * keys)) {
+                    return setError(MLKB_ERR_INVALID, "qk composite: scale map range exceeds S");
+                }
+                MapRoot r;
+                r.begin = loop.begin;
+                r.end = loop.end;
+                r.a = static_cast<int>(mm.out);
+                r.out = static_cast<int>(store->out);
+                r.chain = comp->exprs;
+                m.roots.clear();
+                m.roots.push_back(std::move(r));
                 m.scale = aConst ? e.a_value : e.b_value;
                 m.callA = static_cast<int>(mm.a);
                 m.callB = static_cast<int>(mm.b);
-                m.qkScaled = static_cast<int>(mm.out);
+                m.qkS = static_cast<int>(mm.out);
+                m.qkSc = static_cast<int>(store->out);
+                m.qkFused = sTemp;
                 m.callOut = static_cast<int>(sm.out);
-                m.m = bq.dims[0];
-                m.k = bq.dims[1];
-                m.n = bk.dims[1];
-                m.roots.clear();
+                m.m = rows;
+                m.k = d;
+                m.n = keys;
                 m.kind = MLKB_KIND_QK_SOFTMAX;
                 return okStatus();
             }

@@ -56,11 +56,16 @@ struct Module {
     bool multiDim = false; // the reference isMultiDimModule rule
     std::vector<int> bindable;  // buffer ids in table order (inputs, outputs)
 
-    std::vector<MapRoot> roots;              // MLKB_KIND_MAP
+    std::vector<MapRoot> roots;              // MLKB_KIND_MAP; QK: the scale map
     int callA = -1, callB = -1, callOut = -1;  // Call kinds
     int64_t m = 0, k = 0, n = 0;             // Call shapes (A=[m,k], B=[k,n])
-    double scale = 1.0;                      // MLKB_KIND_QK_SOFTMAX
-    int qkScaled = -1;                       // QK: temp buffer of the scaled scores
+    // MLKB_KIND_QK_SOFTMAX: S = Q*Kt (Call(MatMul), Q = callA [m,k], Kt =
+    // callB [k,n]), Sc = S * scale (the map, roots[0]), Y = softmax(Sc)
+    // (callOut). With S and Sc temps the module is the fused kernel; with
+    // both as outputs the three steps run as the reference runs them.
+    double scale = 1.0;
+    int qkS = -1, qkSc = -1;
+    bool qkFused = false;
 };
 
 // Parses `json` into `out` and classifies it. Returns an MLKB status; the

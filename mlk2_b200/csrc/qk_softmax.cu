@@ -3,8 +3,12 @@
 // The reference has no fused operator: its composition is Call(MatMul) ->
 // scale map -> Call(Softmax) (runtime/src/execution/kernel_buffers.cpp:
 // 1001-1085, :342-402, :290-340), evaluated in f64 with K^T materialised.
-// Q and K are f16 [batch, s, d] row-major here, so K is already the K-major
-// operand the tcgen05 MMA wants: no transpose is materialised.
+// Q is f16 [batch, m, d] row-major. K comes in either of two layouts and
+// neither is ever transposed in memory:
+//   * K  [batch, s, d] (the direct entry): the K-major operand the MMA takes;
+//   * Kt [batch, d, s] (the module route): the reference's MatMul B operand,
+//     [K, N] row-major (kernel_buffers.cpp:1030-1036), which the MMA reads as
+//     an MN-major operand from the same shared-memory ring.
 //
 // Fused kernel (s % 128 == 0, d in {64, 128}); one CTA per SM, persistent
 // over units = (batch, 128-row band). The output write (4 B per score) is the
@@ -98,11 +102,13 @@ __device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
     if (lane == 0) tc::mbar_arrive(bar);
 }
 
-template <int kS>
+// kKt: K arrives as Kt [batch, d, s] (MN-major operand); else K [batch, s, d].
+// m: score rows per batch (Q rows, a multiple of 128); s: keys per batch.
+template <int kS, bool kKt>
 __global__ void __launch_bounds__(kThreads, 1)
 qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k, float* __restrict__ y, int batch,
-                   int s_in, int d, float c2, int* __restrict__ status) {
+                   int m, int s_in, int d, float c2, int* __restrict__ status) {
     const int s = kS != 0 ? kS : s_in;  // row length, a constant where specialised
     // The kernel has no static shared memory, so the dynamic window starts at
     // the 1024-byte aligned base the 128B-swizzled tiles need.
@@ -113,7 +119,7 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
         return;
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bands = s / kRows;
+    const int bands = m / kRows;
     const int units = batch * bands;
     const int chunks = s / kChunk;
     const int dh = d / 64;  // d-halves (1 or 2)
@@ -181,7 +187,7 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
             tc::mbar_arrive_expect_tx(&sm.qfull[slot], kQBox * dh);
             for (int h = 0; h < dh; ++h) {
                 tc::tma_load_2d(sm.q[slot][h], &tma_q, &sm.qfull[slot], h * 64,
-                                b * s + band * kRows);
+                                b * m + band * kRows);
             }
             return true;
         };
@@ -194,7 +200,15 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                     return false;
                 }
                 tc::mbar_arrive_expect_tx(&sm.kfull[st], kKBox);
-                tc::tma_load_2d(sm.k[st], &tma_k, &sm.kfull[st], h * 64, b * s + c * kChunk);
+                if constexpr (kKt) {
+                    // d rows h*64.. of Kt, keys c*128..: two [64 x 64] boxes
+                    // side by side along the keys (MN-major, 128B swizzle)
+                    tc::tma_load_2d(sm.k[st], &tma_k, &sm.kfull[st], c * kChunk, b * d + h * 64);
+                    tc::tma_load_2d(sm.k[st] + kKBox / 2, &tma_k, &sm.kfull[st],
+                                    c * kChunk + 64, b * d + h * 64);
+                } else {
+                    tc::tma_load_2d(sm.k[st], &tma_k, &sm.kfull[st], h * 64, b * s + c * kChunk);
+                }
             }
             return true;
         };
@@ -221,7 +235,16 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
         }
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer ----------------
-        constexpr uint32_t kIdesc = tc::idesc_f16_f32(kRows, kChunk, 0, 0);
+        // Pass 1: Q (A, K-major) x K chunk (B); pass 2 swaps them: K chunk (A)
+        // x Q (B). With Kt the K chunk is the MN-major operand of both.
+        constexpr uint32_t kIdescP1 = tc::idesc_f16_f32(kRows, kChunk, 0, kKt ? 1 : 0);
+        constexpr uint32_t kIdescP2 = tc::idesc_f16_f32(kRows, kChunk, kKt ? 1 : 0, 0);
+        // K16 step kk of a K stage: K-major steps 32 B along the swizzled
+        // row; MN-major steps 16 d-rows (2 KB), the second 64-key box 8 KB on.
+        auto kdesc = [](uint32_t k0, int kk) -> uint64_t {
+            return kKt ? tc::smem_desc_sw128(k0 + kk * 2048, kKBox / 2, 1024)
+                       : tc::smem_desc_sw128(k0 + kk * 32, 16, 1024);
+        };
         uint32_t kit = 0, ait = 0, bit = 0;
         // One accumulator chunk: Q slot x K chunk -> TMEM columns `dst`; with
         // `keys_as_rows` the operands swap and the chunk lands transposed.
@@ -237,9 +260,9 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t dq = tc::smem_desc_sw128(q0 + kk * 32, 16, 1024);
-                    const uint64_t dk = tc::smem_desc_sw128(k0 + kk * 32, 16, 1024);
-                    tc::mma_f16(dst, keys_as_rows ? dk : dq, keys_as_rows ? dq : dk, kIdesc,
-                                (h > 0 || kk > 0) ? 1u : 0u);
+                    const uint64_t dk = kdesc(k0, kk);
+                    tc::mma_f16(dst, keys_as_rows ? dk : dq, keys_as_rows ? dq : dk,
+                                keys_as_rows ? kIdescP2 : kIdescP1, (h > 0 || kk > 0) ? 1u : 0u);
                 }
                 tc::mma_commit(&sm.kempty[st]);
             }
@@ -260,15 +283,13 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                 const uint32_t qa0 = tc::smem_u32(sm.q[qa][h]);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    tc::mma_f16(db, tc::smem_desc_sw128(k0 + kk * 32, 16, 1024),
-                                tc::smem_desc_sw128(qb0 + kk * 32, 16, 1024), kIdesc,
-                                (h > 0 || kk > 0) ? 1u : 0u);
+                    tc::mma_f16(db, kdesc(k0, kk), tc::smem_desc_sw128(qb0 + kk * 32, 16, 1024),
+                                kIdescP2, (h > 0 || kk > 0) ? 1u : 0u);
                 }
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    tc::mma_f16(da, tc::smem_desc_sw128(qa0 + kk * 32, 16, 1024),
-                                tc::smem_desc_sw128(k0 + kk * 32, 16, 1024), kIdesc,
-                                (h > 0 || kk > 0) ? 1u : 0u);
+                    tc::mma_f16(da, tc::smem_desc_sw128(qa0 + kk * 32, 16, 1024), kdesc(k0, kk),
+                                kIdescP1, (h > 0 || kk > 0) ? 1u : 0u);
                 }
                 tc::mma_commit(&sm.kempty[st]);
             }
@@ -394,7 +415,7 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
             if (!tc::mbar_wait(&sm.sfull[slot], (i >> 1) & 1, abort, kLimitNs)) goto b_done;
             const float* const nmi = sm.nmi[slot];
             float* const yband =
-                y + (static_cast<int64_t>(b) * s + band * kRows) * s + quarter * 32 + lane;
+                y + (static_cast<int64_t>(b) * m + band * kRows) * s + quarter * 32 + lane;
             for (int c = 0; c < chunks; ++c, ++bit) {
                 const uint32_t acc = bit & 1u;
                 if (!tc::mbar_wait(&sm.bfull[acc], (bit >> 1) & 1u, abort, kLimitNs)) goto b_done;
@@ -452,31 +473,54 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
 }  // namespace
 }  // namespace mlkb
 
-extern "C" int mlkb_qk_softmax_f16(const void* q, const void* k, float* y, int64_t batch,
-                                   int64_t s, int64_t d, double scale, void* stream) {
-    using namespace mlkb;
+namespace mlkb {
+
+// Y[b] = softmax_rows(scale * Q[b] * K[b]^T) over Q [batch, m, d] and either
+// K [batch, s, d] (kt == false) or Kt [batch, d, s] (kt == true); Y is
+// [batch, m, s]. Fused kernel for m, s multiples of 128 and d in {64, 128};
+// otherwise the two-step form (tcgen05 GEMM with the scale in its epilogue,
+// then the row softmax in place).
+int launchQkSoftmax(const void* q, const void* k, float* y, int64_t batch, int64_t m, int64_t s,
+                    int64_t d, double scale, bool kt, cudaStream_t st) {
     if (q == nullptr || k == nullptr || y == nullptr) {
         return setError(MLKB_ERR_INVALID, "qk_softmax: null buffer");
     }
-    if (batch <= 0 || s <= 0 || d <= 0) {
+    if (batch <= 0 || m <= 0 || s <= 0 || d <= 0) {
         return setError(MLKB_ERR_INVALID, "qk_softmax: shape must be positive");
     }
     if (d % 8 != 0 || s % 8 != 0 || !aligned16(q) || !aligned16(k) || !aligned16(y) ||
-        batch * s > (int64_t(1) << 30)) {
+        batch * m > (int64_t(1) << 30) || batch * s > (int64_t(1) << 30) ||
+        batch * d > (int64_t(1) << 30)) {
         return setError(MLKB_ERR_INVALID,
                         "qk_softmax: d and s must be multiples of 8 with 16-byte aligned buffers");
     }
-    cudaStream_t st = asStream(stream);
-    if (s % kChunk != 0 || (d != 64 && d != 128)) {
-        if (int rc = launchGemmTc(q, k, y, batch, s, s, d, true, 0, static_cast<float>(scale), st)) {
-            return rc;
+    if (m % kRows != 0 || s % kChunk != 0 || (d != 64 && d != 128)) {
+        if (!kt) {
+            if (int rc = launchGemmTc(q, k, y, batch, m, s, d, true, 0,
+                                      static_cast<float>(scale), st)) {
+                return rc;
+            }
+        } else {
+            // One launch per batch: each batch's Kt is its own [d, s] tensor,
+            // so a K tile past d reads zeros, never the next batch's rows.
+            for (int64_t b = 0; b < batch; ++b) {
+                if (int rc = launchGemmTc(static_cast<const __half*>(q) + b * m * d,
+                                          static_cast<const __half*>(k) + b * d * s, y + b * m * s,
+                                          1, m, s, d, false, 0, static_cast<float>(scale), st)) {
+                    return rc;
+                }
+            }
         }
-        return mlkb_softmax_f32(y, y, batch * s, s, stream);
+        return mlkb_softmax_f32(y, y, batch * m, s, st);
     }
     CUtensorMap tq, tk;
-    if (int rc = makeTmapF16(&tq, q, batch * s, d, kRows, 64)) return rc;
-    if (int rc = makeTmapF16(&tk, k, batch * s, d, kChunk, 64)) return rc;
-    static std::atomic<bool> attr[4][64];
+    if (int rc = makeTmapF16(&tq, q, batch * m, d, kRows, 64)) return rc;
+    if (kt) {
+        if (int rc = makeTmapF16(&tk, k, batch * d, s, 64, 64)) return rc;
+    } else {
+        if (int rc = makeTmapF16(&tk, k, batch * s, d, kChunk, 64)) return rc;
+    }
+    static std::atomic<bool> attr[8][64];
     int dev = 0;
     cudaGetDevice(&dev);
     int optin = 0;
@@ -490,25 +534,28 @@ extern "C" int mlkb_qk_softmax_f16(const void* q, const void* k, float* y, int64
     // Row lengths of 1024, 2048 and 4096 get a kernel specialised on them: a
     // pass-2 warp then addresses all 32 rows of a group from one base by
     // immediate offsets instead of stepping a 64-bit pointer per store.
-    const int which = s == 1024 ? 1 : s == 2048 ? 2 : s == 4096 ? 3 : 0;
-    decltype(&qk_softmax_tcgen05<0>) const kern =
-        which == 1 ? qk_softmax_tcgen05<1024>
-        : which == 2 ? qk_softmax_tcgen05<2048>
-        : which == 3 ? qk_softmax_tcgen05<4096>
-                     : qk_softmax_tcgen05<0>;
+    const int len = s == 1024 ? 1 : s == 2048 ? 2 : s == 4096 ? 3 : 0;
+    using Kern = decltype(&qk_softmax_tcgen05<0, false>);
+    static const Kern kKerns[8] = {
+        qk_softmax_tcgen05<0, false>,    qk_softmax_tcgen05<1024, false>,
+        qk_softmax_tcgen05<2048, false>, qk_softmax_tcgen05<4096, false>,
+        qk_softmax_tcgen05<0, true>,     qk_softmax_tcgen05<1024, true>,
+        qk_softmax_tcgen05<2048, true>,  qk_softmax_tcgen05<4096, true>};
+    const int which = len + (kt ? 4 : 0);
+    const Kern kern = kKerns[which];
     if (dev >= 0 && dev < 64 && !attr[which][dev]) {
         const cudaError_t e = cudaFuncSetAttribute(
             kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
         if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "qk smem attribute");
         attr[which][dev] = true;
     }
-    const int64_t units = batch * (s / kRows);
+    const int64_t units = batch * (m / kRows);
     const int grid = static_cast<int>(units < smCount() ? units : smCount());
     // exp(scale * v) = exp2(scale * log2(e) * v)
     const float c2 = static_cast<float>(scale * 1.4426950408889634);
     kern<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, y, static_cast<int>(batch),
-                                             static_cast<int>(s), static_cast<int>(d), c2,
-                                             deviceStatusPtr());
+                                             static_cast<int>(m), static_cast<int>(s),
+                                             static_cast<int>(d), c2, deviceStatusPtr());
     const cudaError_t le = cudaGetLastError();
     if (le != cudaSuccess) {
         cudaFuncAttributes fa{};
@@ -522,4 +569,17 @@ extern "C" int mlkb_qk_softmax_f16(const void* q, const void* k, float* y, int64
         return setError(MLKB_ERR_LAUNCH, msg);
     }
     return okStatus();
+}
+
+}  // namespace mlkb
+
+extern "C" int mlkb_qk_softmax_f16(const void* q, const void* k, float* y, int64_t batch,
+                                   int64_t s, int64_t d, double scale, void* stream) {
+    return mlkb::launchQkSoftmax(q, k, y, batch, s, s, d, scale, false, mlkb::asStream(stream));
+}
+
+extern "C" int mlkb_qk_softmax_kt_f16(const void* q, const void* kt, float* y, int64_t batch,
+                                      int64_t m, int64_t s, int64_t d, double scale,
+                                      void* stream) {
+    return mlkb::launchQkSoftmax(q, kt, y, batch, m, s, d, scale, true, mlkb::asStream(stream));
 }

@@ -143,37 +143,94 @@ int slotPtr(int dev, size_t i, size_t bytes, void** out) {
 
 // ---- module dispatch over device buffers -------------------------------------
 
-// u = x*x + 3x as lowering emits it: Mul(A,A), Mul(3,A), Add(t0,t1).
-bool isU(const std::vector<mlkb_expr>& c) {
-    if (c.size() < 3) return false;
-    const mlkb_expr &e0 = c[0], &e1 = c[1], &e2 = c[2];
-    const bool m0 = e0.op == 2 && e0.a_kind == 1 && e0.b_kind == 1;
-    const bool m1 = e1.op == 2 && ((e1.a_kind == 0 && e1.a_value == 3.0 && e1.b_kind == 1) ||
-                                   (e1.b_kind == 0 && e1.b_value == 3.0 && e1.a_kind == 1));
-    const bool m2 = e2.op == 0 && e2.a_kind == 4 && e2.b_kind == 4 &&
-                    ((e2.a_index == 0 && e2.b_index == 1) || (e2.a_index == 1 && e2.b_index == 0));
-    return m0 && m1 && m2;
+// ---- fast-path recognition ------------------------------------------------------
+// The two dedicated map kernels compute, for f32 x,
+//   y  = sin(u)               u = x*x + 3x
+//   dy = cos(u) * (2x + 3)
+// with the reference's f64 rounding of u. A chain is matched as an expression
+// TREE (temps resolved, Add and Mul commutative), so any expression order a
+// lowering emits is recognised. Only forms equal to these for EVERY f32 x,
+// bit for bit up to the NaN payload, are admitted:
+//   * a+b = b+a and a*b = b*a (IEEE addition and multiplication commute);
+//   * x + x = 2*x (both exact);
+//   * 0*x + 3 inside the derivative: 3 for finite x; for x = +-inf or NaN it
+//     is NaN, and so is cos(u) (u = +inf, NaN or NaN), so the product is NaN
+//     either way. This is the form the reference's calculus.derivative_symbolic
+//     product rule, u'v + uv' (compiler/src/passes/calculus/
+//     calculus.derivative_symbolic.cpp:71-83), leaves after math.canonicalize:
+//     cos(3x + x*x) * ((x + x) + (0*x + 3)).
+namespace fast {
+
+struct Opnd {
+    int kind;
+    int64_t index;
+    double value;
+};
+
+Opnd lhs(const mlkb_expr& e) { return {e.a_kind, e.a_index, e.a_value}; }
+Opnd rhs(const mlkb_expr& e) { return {e.b_kind, e.b_index, e.b_value}; }
+
+bool isX(const Opnd& o) { return o.kind == 1; }
+bool isC(const Opnd& o, double v) { return o.kind == 0 && o.value == v; }
+
+// The expression a Temp operand names (checkChain guarantees idx < k).
+const mlkb_expr* def(const std::vector<mlkb_expr>& c, const Opnd& o) {
+    return (o.kind == 4 && o.index >= 0 && o.index < static_cast<int64_t>(c.size()))
+               ? &c[static_cast<size_t>(o.index)]
+               : nullptr;
 }
+
+template <typename F, typename G>
+bool comm(const std::vector<mlkb_expr>& c, const Opnd& o, int op, F f, G g) {
+    const mlkb_expr* e = def(c, o);
+    if (e == nullptr || e->op != op) return false;
+    return (f(lhs(*e)) && g(rhs(*e))) || (f(rhs(*e)) && g(lhs(*e)));
+}
+
+constexpr int kAddOp = 0, kMulOp = 2, kSinOp = 8, kCosOp = 9;
+
+// u = x*x + 3*x
+bool isU(const std::vector<mlkb_expr>& c, const Opnd& o) {
+    auto xx = [&](const Opnd& p) { return comm(c, p, kMulOp, isX, isX); };
+    auto three_x = [&](const Opnd& p) {
+        return comm(c, p, kMulOp, [](const Opnd& q) { return isC(q, 3.0); }, isX);
+    };
+    return comm(c, o, kAddOp, xx, three_x);
+}
+
+Opnd root(const std::vector<mlkb_expr>& c) {
+    return {4, static_cast<int64_t>(c.size()) - 1, 0.0};
+}
+
+}  // namespace fast
 
 // y = sin(u): the config-1 chain.
 bool isSinChain(const std::vector<mlkb_expr>& c) {
-    return c.size() == 4 && isU(c) && c[3].op == 8 && c[3].a_kind == 4 && c[3].a_index == 2;
+    using namespace fast;
+    const mlkb_expr* e = def(c, root(c));
+    return e != nullptr && e->op == kSinOp && isU(c, lhs(*e));
 }
 
 // dy = cos(u) * (2x + 3): the calculus-pass derivative chain.
 bool isDsinChain(const std::vector<mlkb_expr>& c) {
-    if (c.size() != 7 || !isU(c)) return false;
-    const mlkb_expr &e3 = c[3], &e4 = c[4], &e5 = c[5], &e6 = c[6];
-    const bool cosu = e3.op == 9 && e3.a_kind == 4 && e3.a_index == 2;
-    const bool twox = e4.op == 2 && ((e4.a_kind == 0 && e4.a_value == 2.0 && e4.b_kind == 1) ||
-                                     (e4.b_kind == 0 && e4.b_value == 2.0 && e4.a_kind == 1));
-    const bool plus3 = e5.op == 0 && ((e5.a_kind == 4 && e5.a_index == 4 && e5.b_kind == 0 &&
-                                       e5.b_value == 3.0) ||
-                                      (e5.b_kind == 4 && e5.b_index == 4 && e5.a_kind == 0 &&
-                                       e5.a_value == 3.0));
-    const bool prod = e6.op == 2 && e6.a_kind == 4 && e6.b_kind == 4 &&
-                      ((e6.a_index == 3 && e6.b_index == 5) || (e6.a_index == 5 && e6.b_index == 3));
-    return cosu && twox && plus3 && prod;
+    using namespace fast;
+    auto cosu = [&](const Opnd& p) {
+        const mlkb_expr* e = def(c, p);
+        return e != nullptr && e->op == kCosOp && isU(c, lhs(*e));
+    };
+    auto two_x = [&](const Opnd& p) {
+        return comm(c, p, kMulOp, [](const Opnd& q) { return isC(q, 2.0); }, isX) ||
+               comm(c, p, kAddOp, isX, isX);
+    };
+    auto three = [&](const Opnd& p) {
+        auto zero_x = [&](const Opnd& q) {
+            return comm(c, q, kMulOp, [](const Opnd& r) { return isC(r, 0.0); }, isX);
+        };
+        return isC(p, 3.0) ||
+               comm(c, p, kAddOp, zero_x, [](const Opnd& q) { return isC(q, 3.0); });
+    };
+    auto lin = [&](const Opnd& p) { return comm(c, p, kAddOp, two_x, three); };
+    return comm(c, root(c), kMulOp, cosu, lin);
 }
 
 void* bufAt(void* const* bufs, const Module& m, int bid) {
@@ -194,62 +251,277 @@ char* offsetPtr(void* p, int64_t elems, int dtype) {
     return static_cast<char*>(p) + elems * elemBytes(dtype);
 }
 
-int runMapDev(const Module& m, void* const* bufs, const int32_t* dt, int64_t n,
-              const double* scalars, int64_t n_scalars, void* stream) {
+// Which kernel runs each root of a map module (in root order):
+// kMapSin / kMapSinDsin (the dedicated f32 kernels, the latter also taking
+// root `q`, a derivative root over the same input and range) or kMapChain
+// (the generic chain interpreter).
+enum MapKernel { kMapSin = 1, kMapSinDsin = 2, kMapChain = 3 };
+
+struct MapLaunch {
+    MapKernel kernel;
+    size_t r, q;
+};
+
+std::vector<MapLaunch> planMap(const Module& m, const int32_t* dt) {
+    std::vector<MapLaunch> plan;
     std::vector<uint8_t> done(m.roots.size(), 0);
     for (size_t r = 0; r < m.roots.size(); ++r) {
         if (done[r]) continue;
         const MapRoot& root = m.roots[r];
-        const int64_t end = root.end < 0 ? n : root.end;
-        const int64_t cnt = end > root.begin ? end - root.begin : 0;
+        const int dtOut = dtypeAt(dt, m, root.out);
+        if (dtOut != MLKB_F32 || root.a < 0 || root.poly7 || root.out == root.a ||
+            dtypeAt(dt, m, root.a) != MLKB_F32 || !isSinChain(root.chain)) {
+            plan.push_back({kMapChain, r, r});
+            continue;
+        }
+        // Fuse with a later derivative root over the same input and range,
+        // when no root in between writes x or touches dy (the reference runs
+        // the roots in order, kernel_buffers.cpp:921-953).
+        size_t partner = r;
+        for (size_t q = r + 1; q < m.roots.size() && partner == r; ++q) {
+            const MapRoot& o = m.roots[q];
+            if (done[q] || o.a != root.a || o.begin != root.begin || o.end != root.end ||
+                o.out == root.a || dtypeAt(dt, m, o.out) != MLKB_F32 || !isDsinChain(o.chain)) {
+                continue;
+            }
+            bool clear = true;
+            for (size_t p = r + 1; p < q; ++p) {
+                const MapRoot& mid = m.roots[p];
+                clear = clear && mid.out != root.a && mid.out != o.out && mid.a != o.out &&
+                        mid.b != o.out;
+            }
+            if (clear) partner = q;
+        }
+        if (partner != r) {
+            done[partner] = 1;
+            plan.push_back({kMapSinDsin, r, partner});
+        } else {
+            plan.push_back({kMapSin, r, r});
+        }
+    }
+    return plan;
+}
+
+int runMapDev(const Module& m, void* const* bufs, const int32_t* dt, int64_t n,
+              const double* scalars, int64_t n_scalars, void* stream) {
+    for (const MapRoot& root : m.roots) {
         const int dtOut = dtypeAt(dt, m, root.out);
         const int dtA = root.a >= 0 ? dtypeAt(dt, m, root.a) : dtOut;
         const int dtB = root.b >= 0 ? dtypeAt(dt, m, root.b) : dtOut;
-        void* out = bufAt(bufs, m, root.out);
-        void* a = root.a >= 0 ? bufAt(bufs, m, root.a) : nullptr;
-        void* b = root.b >= 0 ? bufAt(bufs, m, root.b) : nullptr;
-        if (out == nullptr || (root.a >= 0 && a == nullptr) || (root.b >= 0 && b == nullptr)) {
+        if (bufAt(bufs, m, root.out) == nullptr || (root.a >= 0 && bufAt(bufs, m, root.a) == nullptr) ||
+            (root.b >= 0 && bufAt(bufs, m, root.b) == nullptr)) {
             return setError(MLKB_ERR_INVALID, "map: buffer not bound by the caller");
         }
         if (dtA != dtOut || dtB != dtOut || (dtOut != MLKB_F32 && dtOut != MLKB_F64)) {
             return setError(MLKB_ERR_INVALID, "map: buffers must all be f32 or all f64");
         }
+    }
+    for (const MapLaunch& l : planMap(m, dt)) {
+        const MapRoot& root = m.roots[l.r];
+        const int64_t end = root.end < 0 ? n : root.end;
+        const int64_t cnt = end > root.begin ? end - root.begin : 0;
         if (cnt == 0) continue;
-        if (dtOut == MLKB_F32 && root.a >= 0 && !root.poly7 && isSinChain(root.chain)) {
-            // Fuse with a later derivative root over the same input and range.
-            for (size_t q = r + 1; q < m.roots.size(); ++q) {
-                const MapRoot& o = m.roots[q];
-                if (!done[q] && o.a == root.a && o.begin == root.begin && o.end == root.end &&
-                    isDsinChain(o.chain) && dtypeAt(dt, m, o.out) == MLKB_F32 &&
-                    bufAt(bufs, m, o.out) != nullptr) {
-                    done[q] = 1;
-                    int st = mlkb_map_sin_dsin_f32(
-                        reinterpret_cast<const float*>(offsetPtr(a, root.begin, dtA)),
-                        reinterpret_cast<float*>(offsetPtr(out, root.begin, dtOut)),
-                        reinterpret_cast<float*>(offsetPtr(bufAt(bufs, m, o.out), o.begin, dtOut)),
-                        cnt, stream);
-                    if (st) return st;
-                    goto next_root;
-                }
-            }
-            if (int st = mlkb_map_sin_f32(
-                    reinterpret_cast<const float*>(offsetPtr(a, root.begin, dtA)),
-                    reinterpret_cast<float*>(offsetPtr(out, root.begin, dtOut)), cnt, stream)) {
-                return st;
-            }
-            continue;
+        const int dtOut = dtypeAt(dt, m, root.out);
+        void* out = offsetPtr(bufAt(bufs, m, root.out), root.begin, dtOut);
+        void* a = root.a >= 0 ? offsetPtr(bufAt(bufs, m, root.a), root.begin, dtOut) : nullptr;
+        void* b = root.b >= 0 ? offsetPtr(bufAt(bufs, m, root.b), root.begin, dtOut) : nullptr;
+        int st = MLKB_OK;
+        if (l.kernel == kMapSinDsin) {
+            void* dy = offsetPtr(bufAt(bufs, m, m.roots[l.q].out), root.begin, dtOut);
+            st = mlkb_map_sin_dsin_f32(static_cast<const float*>(a), static_cast<float*>(out),
+                                       static_cast<float*>(dy), cnt, stream);
+        } else if (l.kernel == kMapSin) {
+            st = mlkb_map_sin_f32(static_cast<const float*>(a), static_cast<float*>(out), cnt,
+                                  stream);
+        } else {
+            st = mlkb_map_chain(root.chain.data(), static_cast<int32_t>(root.chain.size()),
+                                root.poly7 ? 1 : 0, a, b, out, dtOut, cnt, scalars, n_scalars,
+                                stream);
         }
-        if (int st = mlkb_map_chain(root.chain.data(), static_cast<int32_t>(root.chain.size()),
-                                    root.poly7 ? 1 : 0,
-                                    a != nullptr ? offsetPtr(a, root.begin, dtA) : nullptr,
-                                    b != nullptr ? offsetPtr(b, root.begin, dtB) : nullptr,
-                                    offsetPtr(out, root.begin, dtOut), dtOut, cnt, scalars,
+        if (st) return st;
+    }
+    return okStatus();
+}
+
+// The kernels runDev launches for `m` with these dtypes, comma separated.
+std::string planText(const Module& m, const int32_t* dt) {
+    std::string s;
+    auto add = [&](const char* k) {
+        if (!s.empty()) s += ",";
+        s += k;
+    };
+    auto f = [&](int bid) { return dtypeAt(dt, m, bid); };
+    switch (m.kind) {
+        case MLKB_KIND_MAP:
+            for (const MapLaunch& l : planMap(m, dt)) {
+                add(l.kernel == kMapSinDsin ? "map_sin_dsin_f32"
+                    : l.kernel == kMapSin   ? "map_sin_f32"
+                    : (m.roots[l.r].poly7 ? "map_chain_poly7" : "map_chain"));
+            }
+            break;
+        case MLKB_KIND_SOFTMAX: add(f(m.callA) == MLKB_F64 ? "softmax_f64" : "softmax_f32"); break;
+        case MLKB_KIND_REDUCESUM: add(f(m.callA) == MLKB_F64 ? "reducesum_f64" : "reducesum_f32"); break;
+        case MLKB_KIND_MATMUL:
+            add(f(m.callA) == MLKB_F16 ? "gemm_f16_tcgen05" : f(m.callA) == MLKB_F32 ? "gemm_f32" : "gemm_f64");
+            break;
+        case MLKB_KIND_QK_SOFTMAX:
+            if (m.qkFused) {
+                add("qk_softmax_tcgen05_kt");
+            } else {
+                add(f(m.callA) == MLKB_F16 ? "gemm_f16_tcgen05" : f(m.callA) == MLKB_F32 ? "gemm_f32" : "gemm_f64");
+                add("map_chain");
+                add(f(m.callOut) == MLKB_F64 ? "softmax_f64" : "softmax_f32");
+            }
+            break;
+        default: break;
+    }
+    return s;
+}
+
+int launchRowsKind(bool softmax, void* a, void* y, int dtype, int64_t rows, int64_t cols,
+                   void* stream) {
+    if (dtype == MLKB_F32) {
+        return softmax ? mlkb_softmax_f32(static_cast<float*>(a), static_cast<float*>(y), rows,
+                                          cols, stream)
+                       : mlkb_reducesum_f32(static_cast<float*>(a), static_cast<float*>(y), rows,
+                                            cols, stream);
+    }
+    if (dtype == MLKB_F64) {
+        return softmax ? mlkb_softmax_f64(static_cast<double*>(a), static_cast<double*>(y), rows,
+                                          cols, stream)
+                       : mlkb_reducesum_f64(static_cast<double*>(a), static_cast<double*>(y),
+                                            rows, cols, stream);
+    }
+    return setError(MLKB_ERR_INVALID, "rows: dtype must be f32 or f64");
+}
+
+// C += A * B in the reference's accumulate form (kernel_buffers.cpp:406-432).
+int launchMatmulKind(void* a, void* b, void* c, int da, int db, int dc, int64_t m, int64_t n,
+                     int64_t k, void* stream) {
+    if (da == MLKB_F16 && db == MLKB_F16 && dc == MLKB_F32) {
+        return mlkb_gemm_f16_f32(a, b, static_cast<float*>(c), m, n, k, 1, stream);
+    }
+    if (da == MLKB_F32 && db == MLKB_F32 && dc == MLKB_F32) {
+        return mlkb_gemm_f32(static_cast<float*>(a), static_cast<float*>(b),
+                             static_cast<float*>(c), m, n, k, 1, stream);
+    }
+    if (da == MLKB_F64 && db == MLKB_F64 && dc == MLKB_F64) {
+        return mlkb_gemm_f64(static_cast<double*>(a), static_cast<double*>(b),
+                             static_cast<double*>(c), m, n, k, 1, stream);
+    }
+    return setError(MLKB_ERR_INVALID, "matmul: dtypes must be f16/f16/f32, f32 or f64");
+}
+
+// The scaled-scores composite (module.h). Fused form: S and Sc are temps, so
+// S starts at zero, the scale map covers all of S, and Y is the only result.
+// Output form: the reference's three steps, each on the device.
+int runQkDev(const Module& m, void* const* bufs, const int32_t* dt, int64_t n,
+             const double* scalars, int64_t n_scalars, void* stream) {
+    void* q = bufAt(bufs, m, m.callA);
+    void* kt = bufAt(bufs, m, m.callB);
+    void* y = bufAt(bufs, m, m.callOut);
+    const int dq = dtypeAt(dt, m, m.callA), dk = dtypeAt(dt, m, m.callB),
+              dy = dtypeAt(dt, m, m.callOut);
+    if (q == nullptr || kt == nullptr || y == nullptr) {
+        return setError(MLKB_ERR_INVALID, "qk composite: buffer not bound by the caller");
+    }
+    const MapRoot& r = m.roots[0];
+    const int64_t cells = m.m * m.n;
+    const int64_t end = r.end < 0 ? n : r.end;
+    if (r.begin < 0 || end > cells) {
+        return setError(MLKB_ERR_INVALID, "qk composite: scale map range exceeds S");
+    }
+    if (m.qkFused) {
+        if (r.begin != 0 || end != cells) {
+            return setError(MLKB_ERR_UNSUPPORTED,
+                            "qk composite: with temp scores the scale map must cover all of S");
+        }
+        if (dq != MLKB_F16 || dk != MLKB_F16 || dy != MLKB_F32) {
+            return setError(MLKB_ERR_UNSUPPORTED,
+                            "qk composite with temp scores: Q, Kt f16 and Y f32 required");
+        }
+        return launchQkSoftmax(q, kt, static_cast<float*>(y), 1, m.m, m.n, m.k, m.scale, true,
+                               asStream(stream));
+    }
+    void* sbuf = bufAt(bufs, m, m.qkS);
+    void* scbuf = bufAt(bufs, m, m.qkSc);
+    const int ds = dtypeAt(dt, m, m.qkS), dsc = dtypeAt(dt, m, m.qkSc);
+    if (sbuf == nullptr || scbuf == nullptr) {
+        return setError(MLKB_ERR_INVALID, "qk composite: S or Sc not bound by the caller");
+    }
+    if (ds != dy || dsc != dy) {
+        return setError(MLKB_ERR_INVALID, "qk composite: S, Sc and Y must share one dtype");
+    }
+    if (int st = launchMatmulKind(q, kt, sbuf, dq, dk, ds, m.m, m.n, m.k, stream)) return st;
+    if (end > r.begin) {
+        if (int st = mlkb_map_chain(r.chain.data(), static_cast<int32_t>(r.chain.size()), 0,
+                                    offsetPtr(sbuf, r.begin, ds), nullptr,
+                                    offsetPtr(scbuf, r.begin, dsc), dsc, end - r.begin, scalars,
                                     n_scalars, stream)) {
             return st;
         }
-    next_root:;
     }
-    return okStatus();
+    return launchRowsKind(true, scbuf, y, dsc, m.m, m.n, stream);
+}
+
+// Host-side checks of a run request, before any device work: the dtype
+// combinations each kind runs with, and the ranges the scaled-scores
+// composite needs. The same conditions hold inside runDev.
+int validateRun(const Module& m, const int32_t* dt, int64_t n) {
+    auto f = [&](int bid) { return dtypeAt(dt, m, bid); };
+    switch (m.kind) {
+        case MLKB_KIND_MAP:
+            for (const MapRoot& r : m.roots) {
+                const int o = f(r.out);
+                if ((o != MLKB_F32 && o != MLKB_F64) || (r.a >= 0 && f(r.a) != o) ||
+                    (r.b >= 0 && f(r.b) != o)) {
+                    return setError(MLKB_ERR_INVALID, "map: buffers must all be f32 or all f64");
+                }
+            }
+            return okStatus();
+        case MLKB_KIND_SOFTMAX:
+        case MLKB_KIND_REDUCESUM:
+            if (f(m.callA) != f(m.callOut) || (f(m.callA) != MLKB_F32 && f(m.callA) != MLKB_F64)) {
+                return setError(MLKB_ERR_INVALID, "rows: dtypes must be both f32 or both f64");
+            }
+            return okStatus();
+        case MLKB_KIND_MATMUL: {
+            const int a = f(m.callA), b = f(m.callB), c = f(m.callOut);
+            if (!((a == MLKB_F16 && b == MLKB_F16 && c == MLKB_F32) ||
+                  (a == MLKB_F32 && b == MLKB_F32 && c == MLKB_F32) ||
+                  (a == MLKB_F64 && b == MLKB_F64 && c == MLKB_F64))) {
+                return setError(MLKB_ERR_INVALID, "matmul: dtypes must be f16/f16/f32, f32 or f64");
+            }
+            return okStatus();
+        }
+        case MLKB_KIND_QK_SOFTMAX: {
+            const MapRoot& r = m.roots[0];
+            const int64_t cells = m.m * m.n;
+            const int64_t end = r.end < 0 ? n : r.end;
+            if (end > cells) return setError(MLKB_ERR_INVALID, "qk composite: scale map range exceeds S");
+            const int q = f(m.callA), k = f(m.callB), y = f(m.callOut);
+            if (m.qkFused) {
+                if (r.begin != 0 || end != cells) {
+                    return setError(MLKB_ERR_UNSUPPORTED,
+                                    "qk composite: with temp scores the scale map must cover all of S");
+                }
+                if (q != MLKB_F16 || k != MLKB_F16 || y != MLKB_F32) {
+                    return setError(MLKB_ERR_UNSUPPORTED,
+                                    "qk composite with temp scores: Q, Kt f16 and Y f32 required");
+                }
+                return okStatus();
+            }
+            const int sc = f(m.qkS), scc = f(m.qkSc);
+            const bool ok = ((q == MLKB_F16 && k == MLKB_F16 && y == MLKB_F32) ||
+                             (q == MLKB_F32 && k == MLKB_F32 && y == MLKB_F32) ||
+                             (q == MLKB_F64 && k == MLKB_F64 && y == MLKB_F64)) &&
+                            sc == y && scc == y;
+            return ok ? okStatus()
+                      : setError(MLKB_ERR_INVALID,
+                                 "qk composite: Q/Kt f16, f32 or f64 with S, Sc, Y f32 (f64 for f64)");
+        }
+        default: return setError(MLKB_ERR_UNSUPPORTED, "module kind not runnable here");
+    }
 }
 
 int runDev(const Module& m, void* const* bufs, const int32_t* dt, int64_t n,
@@ -258,45 +530,17 @@ int runDev(const Module& m, void* const* bufs, const int32_t* dt, int64_t n,
         case MLKB_KIND_MAP: return runMapDev(m, bufs, dt, n, scalars, n_scalars, stream);
         case MLKB_KIND_SOFTMAX:
         case MLKB_KIND_REDUCESUM: {
-            void* a = bufAt(bufs, m, m.callA);
-            void* y = bufAt(bufs, m, m.callOut);
             const int da = dtypeAt(dt, m, m.callA), dy = dtypeAt(dt, m, m.callOut);
             if (da != dy) return setError(MLKB_ERR_INVALID, "rows: dtype mismatch");
-            const bool sm = m.kind == MLKB_KIND_SOFTMAX;
-            if (da == MLKB_F32) {
-                return sm ? mlkb_softmax_f32(static_cast<float*>(a), static_cast<float*>(y), m.m,
-                                             m.k, stream)
-                          : mlkb_reducesum_f32(static_cast<float*>(a), static_cast<float*>(y),
-                                               m.m, m.k, stream);
-            }
-            if (da == MLKB_F64) {
-                return sm ? mlkb_softmax_f64(static_cast<double*>(a), static_cast<double*>(y),
-                                             m.m, m.k, stream)
-                          : mlkb_reducesum_f64(static_cast<double*>(a), static_cast<double*>(y),
-                                               m.m, m.k, stream);
-            }
-            return setError(MLKB_ERR_INVALID, "rows: dtype must be f32 or f64");
+            return launchRowsKind(m.kind == MLKB_KIND_SOFTMAX, bufAt(bufs, m, m.callA),
+                                  bufAt(bufs, m, m.callOut), da, m.m, m.k, stream);
         }
-        case MLKB_KIND_MATMUL: {
-            void* a = bufAt(bufs, m, m.callA);
-            void* b = bufAt(bufs, m, m.callB);
-            void* c = bufAt(bufs, m, m.callOut);
-            const int da = dtypeAt(dt, m, m.callA), db = dtypeAt(dt, m, m.callB),
-                      dc = dtypeAt(dt, m, m.callOut);
-            // The reference accumulates: C += A*B (kernel_buffers.cpp:406-432).
-            if (da == MLKB_F16 && db == MLKB_F16 && dc == MLKB_F32) {
-                return mlkb_gemm_f16_f32(a, b, static_cast<float*>(c), m.m, m.n, m.k, 1, stream);
-            }
-            if (da == MLKB_F32 && db == MLKB_F32 && dc == MLKB_F32) {
-                return mlkb_gemm_f32(static_cast<float*>(a), static_cast<float*>(b),
-                                     static_cast<float*>(c), m.m, m.n, m.k, 1, stream);
-            }
-            if (da == MLKB_F64 && db == MLKB_F64 && dc == MLKB_F64) {
-                return mlkb_gemm_f64(static_cast<double*>(a), static_cast<double*>(b),
-                                     static_cast<double*>(c), m.m, m.n, m.k, 1, stream);
-            }
-            return setError(MLKB_ERR_INVALID, "matmul: dtypes must be f16/f16/f32, f32 or f64");
-        }
+        case MLKB_KIND_MATMUL:
+            return launchMatmulKind(bufAt(bufs, m, m.callA), bufAt(bufs, m, m.callB),
+                                    bufAt(bufs, m, m.callOut), dtypeAt(dt, m, m.callA),
+                                    dtypeAt(dt, m, m.callB), dtypeAt(dt, m, m.callOut), m.m,
+                                    m.n, m.k, stream);
+        case MLKB_KIND_QK_SOFTMAX: return runQkDev(m, bufs, dt, n, scalars, n_scalars, stream);
         default: return setError(MLKB_ERR_UNSUPPORTED, "module kind not runnable here");
     }
 }
@@ -309,16 +553,36 @@ struct Shard {
     int64_t u0, u1;
 };
 
-// Split axis per kind: map -> elements of the loop range; rows -> rows of A;
-// matmul -> rows of A and C (B replicated).
+// Split axis per kind: map -> elements of the roots' ranges (the largest
+// end, a static bound or the caller's n, as the executor takes them,
+// kernel_buffers.cpp:924-928); rows -> rows of A; matmul -> rows of A and C
+// (B replicated); scaled scores -> rows of Q, S, Sc and Y (Kt replicated).
+// -1 for a kind no shard runs.
 int64_t unitsOf(const Module& m, int64_t n) {
     switch (m.kind) {
-        case MLKB_KIND_MAP: return n;
+        case MLKB_KIND_MAP: {
+            int64_t u = 0;
+            for (const MapRoot& r : m.roots) {
+                const int64_t end = r.end < 0 ? n : r.end;
+                if (end > u) u = end;
+            }
+            return u;
+        }
         case MLKB_KIND_MATMUL:
         case MLKB_KIND_SOFTMAX:
-        case MLKB_KIND_REDUCESUM: return m.m;
-        default: return 0;
+        case MLKB_KIND_REDUCESUM:
+        case MLKB_KIND_QK_SOFTMAX: return m.m;
+        default: return -1;
     }
+}
+
+// Shard boundary d of g over `units`: contiguous and balanced; the fused
+// scaled-scores kernel keeps its 128-row bands whole.
+int64_t shardEdge(const Module& m, int64_t units, int d, int g) {
+    if (d >= g) return units;
+    int64_t e = units * d / g;
+    if (m.kind == MLKB_KIND_QK_SOFTMAX && m.qkFused && units % 128 == 0) e = e / 128 * 128;
+    return e;
 }
 
 // Runs one shard on its device: stage, run, copy back. Maps stream in chunks
@@ -332,7 +596,7 @@ int runShard(const Module& m0, const Shard& sh, void* const* bufs, const int32_t
     if (int st = ensureCtx(sh.dev)) return st;
     const size_t nb = m0.bindable.size();
     const int64_t units = sh.u1 - sh.u0;
-    if (units <= 0) return okStatus();
+    if (units <= 0) return okStatus();  // an empty shard has nothing to move
 
     if (m0.kind == MLKB_KIND_MAP) {
         // Every root reads/writes element i of its buffers: shard = element range.
@@ -348,12 +612,28 @@ int runShard(const Module& m0, const Shard& sh, void* const* bufs, const int32_t
                 }
             }
         }
+        // How far each buffer reaches: the largest effective end of the roots
+        // that read or write it. Copies never go past it, so a root with a
+        // short static range never touches host memory beyond its own range.
+        std::vector<int64_t> ext(nb, 0);
+        for (const MapRoot& r : m0.roots) {
+            const int64_t rEnd = r.end < 0 ? n : r.end;
+            for (size_t i = 0; i < nb; ++i) {
+                const int bid = m0.bindable[i];
+                if ((bid == r.out || bid == r.a || bid == r.b) && rEnd > ext[i]) ext[i] = rEnd;
+            }
+        }
         // Shift the module's loop ranges into chunk-local coordinates.
         int step = 0;
         for (int64_t base = sh.u0; base < sh.u1; base += chunk, ++step) {
             const int64_t cnt = (sh.u1 - base) < chunk ? (sh.u1 - base) : chunk;
             const int s = step & 1;
             cudaStream_t st = c.streams[s];
+            std::vector<int64_t> vcnt(nb, 0);  // elements of buffer i inside this chunk
+            for (size_t i = 0; i < nb; ++i) {
+                const int64_t v = ext[i] - base;
+                vcnt[i] = v <= 0 ? 0 : (v < cnt ? v : cnt);
+            }
             Module m = m0;
             bool any = false;
             // Per bindable buffer: written by some root in this chunk, and
@@ -370,25 +650,25 @@ int runShard(const Module& m0, const Shard& sh, void* const* bufs, const int32_t
                 for (size_t i = 0; i < nb; ++i) {
                     if (m0.bindable[i] != r.out) continue;
                     written[i] = 1;
-                    if (lo != base || hi != base + cnt) partial[i] = 1;
+                    if (lo != base || hi != base + vcnt[i]) partial[i] = 1;
                 }
             }
             if (!any) continue;
             for (size_t i = 0; i < nb; ++i) {
                 // Inputs, and outputs a root writes only in part (the rest
                 // keeps the caller's values, as in the reference executor).
-                if (m0.buffers[m0.bindable[i]].input || partial[i]) {
+                if ((m0.buffers[m0.bindable[i]].input || partial[i]) && vcnt[i] > 0) {
                     e = cudaMemcpyAsync(dbuf[s][i], offsetPtr(bufs[i], base, dt[i]),
-                                        static_cast<size_t>(cnt) * elemBytes(dt[i]),
+                                        static_cast<size_t>(vcnt[i]) * elemBytes(dt[i]),
                                         cudaMemcpyHostToDevice, st);
                     if (e != cudaSuccess) return setCudaError(MLKB_ERR_CUDA_MEM, e, "H2D");
                 }
             }
             if (int rs = runDev(m, dbuf[s].data(), dt, cnt, scalars, n_scalars, st)) return rs;
             for (size_t i = 0; i < nb; ++i) {
-                if (!written[i]) continue;
+                if (!written[i] || vcnt[i] == 0) continue;
                 e = cudaMemcpyAsync(offsetPtr(bufs[i], base, dt[i]), dbuf[s][i],
-                                    static_cast<size_t>(cnt) * elemBytes(dt[i]),
+                                    static_cast<size_t>(vcnt[i]) * elemBytes(dt[i]),
                                     cudaMemcpyDeviceToHost, st);
                 if (e != cudaSuccess) return setCudaError(MLKB_ERR_CUDA_MEM, e, "D2H");
             }
@@ -400,9 +680,22 @@ int runShard(const Module& m0, const Shard& sh, void* const* bufs, const int32_t
         return okStatus();
     }
 
-    // Row-split kinds: A rows [u0,u1), output rows [u0,u1); MatMul replicates B.
+    // Row-split kinds: A rows [u0,u1), output rows [u0,u1); MatMul replicates
+    // B; the scaled-scores composite replicates Kt and splits Q, S, Sc, Y.
     Module m = m0;
     m.m = units;
+    const bool qk = m.kind == MLKB_KIND_QK_SOFTMAX;
+    bool scPartial = false;
+    if (qk) {
+        // The scale map's flat range over S, clipped to this shard's rows.
+        MapRoot& r = m.roots[0];
+        const int64_t lo0 = r.begin, hi0 = r.end < 0 ? n : r.end;
+        const int64_t base = sh.u0 * m.n, top = sh.u1 * m.n;
+        const int64_t lo = lo0 > base ? lo0 : base, hi = hi0 < top ? hi0 : top;
+        r.begin = hi > lo ? lo - base : 0;
+        r.end = hi > lo ? hi - base : 0;
+        scPartial = r.begin != 0 || r.end != units * m.n;
+    }
     cudaStream_t st = c.streams[0];
     std::vector<void*> dbuf(nb);
     std::vector<int64_t> off(nb, 0), cnt(nb, 0);
@@ -410,8 +703,9 @@ int runShard(const Module& m0, const Shard& sh, void* const* bufs, const int32_t
         const int bid = m.bindable[i];
         int64_t rowLen = 1;
         if (bid == m.callA) rowLen = m.k;
-        else if (bid == m.callOut) rowLen = m.kind == MLKB_KIND_MATMUL ? m.n
+        else if (bid == m.callOut) rowLen = (m.kind == MLKB_KIND_MATMUL || qk) ? m.n
                                             : m.kind == MLKB_KIND_SOFTMAX ? m.k : 1;
+        else if (qk && (bid == m.qkS || bid == m.qkSc)) rowLen = m.n;
         if (bid == m.callB) {
             off[i] = 0;
             cnt[i] = m.k * m.n;
@@ -422,9 +716,12 @@ int runShard(const Module& m0, const Shard& sh, void* const* bufs, const int32_t
         if (int s2 = slotPtr(sh.dev, i, static_cast<size_t>(cnt[i]) * elemBytes(dt[i]), &dbuf[i])) {
             return s2;
         }
-        // Inputs, and MatMul's C (accumulated into), go to the device.
-        const bool stage = m.buffers[bid].input || (m.kind == MLKB_KIND_MATMUL && bid == m.callOut);
-        if (stage) {
+        // Inputs, and every buffer a step accumulates into or writes only in
+        // part, go to the device: MatMul's C (C += A*B), the composite's S
+        // (likewise) and its Sc when the scale map covers only part of it.
+        const bool accumulated = (m.kind == MLKB_KIND_MATMUL && bid == m.callOut) ||
+                                 (qk && bid == m.qkS) || (qk && scPartial && bid == m.qkSc);
+        if (m.buffers[bid].input || accumulated) {
             e = cudaMemcpyAsync(dbuf[i], offsetPtr(bufs[i], off[i], dt[i]),
                                 static_cast<size_t>(cnt[i]) * elemBytes(dt[i]),
                                 cudaMemcpyHostToDevice, st);
@@ -452,11 +749,13 @@ int runHost(const Module& m, void* const* bufs, const int32_t* dt, int32_t n_buf
         if (bufs[i] == nullptr) return setError(MLKB_ERR_INVALID, "run: null host buffer");
         if (elemBytes(dt[i]) == 0) return setError(MLKB_ERR_INVALID, "run: unknown dtype");
     }
+    if (int st = validateRun(m, dt, n)) return st;
     const int avail = deviceCount();
     if (avail <= 0) return setError(MLKB_ERR_NO_DEVICE, "no CUDA device");
     int g = n_gpus <= 0 ? avail : (n_gpus < avail ? n_gpus : avail);
     const int64_t units = unitsOf(m, n);
-    if (units <= 0) return okStatus();
+    if (units < 0) return setError(MLKB_ERR_UNSUPPORTED, "run_host: module kind not runnable here");
+    if (units == 0) return okStatus();  // every loop range is empty: nothing to do
     if (g > units) g = static_cast<int>(units);
     if (g == 1) {
         // One GPU: the caller's current device (one process per GPU).
@@ -466,8 +765,10 @@ int runHost(const Module& m, void* const* bufs, const int32_t* dt, int32_t n_buf
     }
     std::vector<Shard> shards;
     for (int d = 0; d < g; ++d) {
-        shards.push_back(Shard{d, units * d / g, units * (d + 1) / g});
+        const int64_t u0 = shardEdge(m, units, d, g), u1 = shardEdge(m, units, d + 1, g);
+        if (u1 > u0) shards.push_back(Shard{d, u0, u1});
     }
+    g = static_cast<int>(shards.size());
     std::vector<int> rc(g, 0);
     std::vector<std::string> msg(g);
     std::vector<std::thread> th;
@@ -487,6 +788,8 @@ int runHost(const Module& m, void* const* bufs, const int32_t* dt, int32_t n_buf
 // ---- reference artifact ABI state --------------------------------------------
 std::mutex g_bindMu;
 std::shared_ptr<mlkb_module> g_bound;
+int g_bindStatus = MLKB_OK;  // status of the last mlk_bind_module call
+std::string g_bindError;
 std::once_flag g_sidecarOnce;
 
 void loadSidecar() {
@@ -560,6 +863,7 @@ extern "C" int mlkb_module_run_dev(const mlkb_module* module, void* const* bufs,
         return setError(MLKB_ERR_INVALID, "run_dev: buffer count differs from the module table");
     }
     if (n < 0) return setError(MLKB_ERR_INVALID, "run_dev: negative element count");
+    if (int st = validateRun(module->m, dtypes, n)) return st;
     const int avail = deviceCount();
     if (avail <= 0) return setError(MLKB_ERR_NO_DEVICE, "no CUDA device");
     if (device < 0 || device >= avail) return setError(MLKB_ERR_INVALID, "run_dev: bad device");
@@ -580,13 +884,33 @@ extern "C" int mlkb_module_run_host(const mlkb_module* module, void* const* bufs
 
 extern "C" int mlk_bind_module(const char* json) {
     std::lock_guard<std::mutex> lock(g_bindMu);
-    if (json == nullptr) {
-        g_bound.reset();
-        return okStatus();
-    }
+    g_bound.reset();  // a failed bind leaves nothing bound, never the previous module
+    g_bindStatus = okStatus();
+    g_bindError.clear();
+    if (json == nullptr) return okStatus();
     auto mod = std::make_shared<mlkb_module>();
-    if (int st = parseModule(json, mod->m)) return st;
+    if (int st = parseModule(json, mod->m)) {
+        g_bindStatus = st;
+        g_bindError = mlkb_last_error();
+        return st;
+    }
     g_bound = mod;
+    return okStatus();
+}
+
+extern "C" int mlkb_module_plan(const mlkb_module* module, const int32_t* dtypes,
+                                int32_t n_bufs, char* buf, int64_t cap) {
+    if (module == nullptr || dtypes == nullptr || buf == nullptr || cap <= 0) {
+        return setError(MLKB_ERR_INVALID, "module_plan: null argument");
+    }
+    if (n_bufs != static_cast<int32_t>(module->m.bindable.size())) {
+        return setError(MLKB_ERR_INVALID, "module_plan: buffer count differs from the module table");
+    }
+    const std::string s = planText(module->m, dtypes);
+    if (static_cast<int64_t>(s.size()) + 1 > cap) {
+        return setError(MLKB_ERR_INVALID, "module_plan: buffer too small");
+    }
+    std::memcpy(buf, s.c_str(), s.size() + 1);
     return okStatus();
 }
 
@@ -603,7 +927,11 @@ extern "C" int mlk_kernel(intptr_t a0, intptr_t a1, intptr_t a2, intptr_t a3, in
         mod = g_bound;
     }
     if (!mod) {
-        t_status = setError(MLKB_ERR_NOT_BOUND, "mlk_kernel: no module bound");
+        std::lock_guard<std::mutex> lock(g_bindMu);
+        t_status = g_bindStatus != MLKB_OK
+                       ? setError(g_bindStatus, ("mlk_kernel: the bound module was rejected: " +
+                                                 g_bindError).c_str())
+                       : setError(MLKB_ERR_NOT_BOUND, "mlk_kernel: no module bound");
         return t_status;
     }
     const intptr_t args[18] = {a0, a1, a2, a3, a4, a5, a6, a7, a8,
@@ -631,7 +959,10 @@ extern "C" int mlk_kernel(intptr_t a0, intptr_t a1, intptr_t a2, intptr_t a3, in
         scalars = reinterpret_cast<const double*>(args[nb + 1]);
         nsc = static_cast<int64_t>(args[nb + 2]);
     }
-    if (nsc < 0 || nsc > 64) nsc = 0;
+    if (nsc < 0 || (nsc > 0 && scalars == nullptr)) {
+        t_status = setError(MLKB_ERR_INVALID, "mlk_kernel: bad scalar table");
+        return t_status;
+    }
     t_status = runHost(m, bufs.data(), dt.data(), static_cast<int32_t>(nb), n, scalars, nsc, 0);
     return t_status;
 }

@@ -129,24 +129,88 @@ def call_module(kind: str, m: int, k: int, n: int = 0, dtypes=("f32", "f32", "f3
             "nodes": [call], "schedule": {}}
 
 
-def qk_softmax_module(s: int, d: int, scale: float) -> dict:
-    """The scaled-scores softmax composite: Call(MatMul)(Q[s,d], Kt[d,s]) -> S,
+def qk_softmax_module(s: int, d: int, scale: float, temps: bool = False, m: int = 0,
+                      dtype: str = "f16") -> dict:
+    """The scaled-scores softmax composite: Call(MatMul)(Q[m,d], Kt[d,s]) -> S,
     Loop{Sc = S * scale}, Call(Softmax)(Sc) -> Y (reference composition of
-    kernel_buffers.cpp:1001-1085, :342-402 and :290-340)."""
-    bufs = [_buf("Q", "f16", True, [s, d]), _buf("Kt", "f16", True, [d, s]),
-            _buf("S", "f32", False, [s, s]), _buf("Sc", "f32", False, [s, s]),
-            _buf("Y", "f32", False, [s, s])]
+    kernel_buffers.cpp:1001-1085, :342-402 and :290-340). m defaults to s.
+
+    temps=False: S and Sc are outputs (table Q, Kt, S, Sc, Y), the form the
+    reference executor runs; MatMul accumulates into S (S += Q*Kt).
+    temps=True: S and Sc are temps after the outputs (table Q, Kt, Y, S, Sc),
+    only Y is observable -- the fused kernel's form. (The reference's 1-D
+    executor does not bind temps to a Call, kernel_buffers.cpp:219-230, so
+    only this path runs that form.)"""
+    m = m or s
+    io = "f64" if dtype == "f64" else "f32"
+    q, kt = _buf("Q", dtype, True, [m, d]), _buf("Kt", dtype, True, [d, s])
+    sb, scb, yb = (_buf("S", io, False, [m, s]), _buf("Sc", io, False, [m, s]),
+                   _buf("Y", io, False, [m, s]))
+    if temps:
+        for b in (sb, scb):
+            b["output"] = False
+            b["temp"] = True
+        bufs, S_, SC_, Y_ = [q, kt, yb, sb, scb], 3, 4, 2
+    else:
+        bufs, S_, SC_, Y_ = [q, kt, sb, scb, yb], 2, 3, 4
     nodes = [
-        {"op": "call", "begin": 0, "end": -1, "step": 1, "a": 0, "b": 1, "out": 2, "children": []},
+        {"op": "call", "begin": 0, "end": -1, "step": 1, "a": 0, "b": 1, "out": S_, "children": []},
         {"op": "loop", "var": "i", "begin": 0, "end": -1, "step": 1, "parallel": True,
          "children": [2, 3]},
-        {"op": "compute", "math": "mul", "begin": 0, "end": -1, "step": 1, "a": 2,
+        {"op": "compute", "math": "mul", "begin": 0, "end": -1, "step": 1, "a": S_,
          "exprs": [_expr_json(chain(E("mul", A, C(scale)))[0])], "children": []},
-        {"op": "store", "begin": 0, "end": -1, "step": 1, "out": 3, "children": []},
-        {"op": "call", "begin": 0, "end": -1, "step": 1, "a": 3, "out": 4, "children": []},
+        {"op": "store", "begin": 0, "end": -1, "step": 1, "out": SC_, "children": []},
+        {"op": "call", "begin": 0, "end": -1, "step": 1, "a": SC_, "out": Y_, "children": []},
     ]
     return {"format": "mlk-kernel", "version": 1, "name": "qk_softmax", "buffers": bufs,
             "nodes": nodes, "schedule": {}}
+
+
+def merge_roots(modules, names=None) -> dict:
+    """One multi-root module from single-output modules over the same input:
+    buffer 0 of each (its input) becomes the shared input, each module's
+    output its own output buffer, and every node keeps its structure with
+    buffer ids and children renumbered. This is the two-output form the
+    reference's lowering cannot emit itself (lower.to_kernel_ir.cpp:404-408
+    stores every output into outputBuffers[0])."""
+    first = modules[0]
+    bufs = [dict(first["buffers"][0])]
+    nodes = []
+    for r, mod in enumerate(modules):
+        assert mod["buffers"][0]["input"] and sum(b["output"] for b in mod["buffers"]) == 1
+        out = dict(next(b for b in mod["buffers"] if b["output"]))
+        if names is not None:
+            out["name"] = names[r]
+        bufs.append(out)
+        remap = {0: 0, next(i for i, b in enumerate(mod["buffers"]) if b["output"]): len(bufs) - 1}
+        base = len(nodes)
+        for n in mod["nodes"]:
+            n = json.loads(json.dumps(n))
+            for k in ("a", "b", "out"):
+                if k in n:
+                    n[k] = remap[n[k]]
+            n["children"] = [c + base for c in n.get("children", [])]
+            nodes.append(n)
+    return {"format": "mlk-kernel", "version": first.get("version", 1), "name": "fused_map",
+            "buffers": bufs, "nodes": nodes, "schedule": dict(first.get("schedule", {}))}
+
+
+def chains_of(module: dict):
+    """The expression chain of each Compute node, as mlkb_expr arrays (for
+    running a module's chains through the oracle)."""
+    out = []
+    for n in module["nodes"]:
+        if n["op"] != "compute":
+            continue
+        rows = []
+        for e in n["exprs"]:
+            ops = []
+            for side in ("a", "b"):
+                o = e.get(side, {"kind": "const", "value": 0.0})
+                ops.append((KINDS.index(o["kind"]), int(o.get("index", 0)), float(o.get("value", 0.0))))
+            rows.append((OP[e["op"]], ops[0][0], ops[0][1], ops[0][2], ops[1][0], 0, ops[1][1], ops[1][2]))
+        out.append(np.array(rows, dtype=EXPR_DTYPE))
+    return out
 
 
 def dumps(module: dict) -> str:

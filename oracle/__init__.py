@@ -30,16 +30,15 @@ def _p(a):
 class _Executor:
     """Common ctypes surface of the port and the compiled reference."""
 
-    def __init__(self, path: str, prefix: str, chain_has_poly7: bool):
+    def __init__(self, path: str, prefix: str):
         self.path = path
         self.lib = C.CDLL(path)
         self.prefix = prefix
-        self._poly7 = chain_has_poly7
         f = self._fn
-        if chain_has_poly7:
+        if prefix == "mlkref_":
             f("chain").argtypes = [_i32, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _vp, _i64, _i64]
         else:
-            f("chain").argtypes = [_i32, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64]
+            f("chain").argtypes = [_i32, _vp, _vp, _i32, _vp, _vp, _vp, _i64, _vp, _i64]
         for name in ("softmax", "reducesum"):
             f(name).argtypes = [_vp, _vp, _i64, _i64]
         if prefix == "mlkref_":
@@ -70,13 +69,13 @@ class _Executor:
         outs = [np.zeros(a.size, np.float64) for _ in chains]
         optr = (C.c_void_p * len(outs))(*[o.ctypes.data for o in outs])
         sc = np.ascontiguousarray(scalars, dtype=np.float64)
-        if self._poly7:
+        if self.prefix == "mlkref_":
             rc = self._fn("chain")(len(chains), lens, allx.ctypes.data, int(poly7), _p(a), _p(b),
                                    optr, a.size, sc.ctypes.data if sc.size else None, sc.size,
                                    threads)
         else:
-            rc = self._fn("chain")(len(chains), lens, allx.ctypes.data, _p(a), _p(b), optr,
-                                   a.size, sc.ctypes.data if sc.size else None, sc.size)
+            rc = self._fn("chain")(len(chains), lens, allx.ctypes.data, int(poly7), _p(a), _p(b),
+                                   optr, a.size, sc.ctypes.data if sc.size else None, sc.size)
         self._check(rc)
         return outs
 
@@ -113,7 +112,7 @@ _ref = None
 def port() -> _Executor:
     global _port
     if _port is None:
-        _port = _Executor(PORT_PATH, "mlko_", False)
+        _port = _Executor(PORT_PATH, "mlko_")
     return _port
 
 
@@ -124,8 +123,41 @@ def ref_available() -> bool:
 def ref() -> _Executor:
     global _ref
     if _ref is None:
-        _ref = _Executor(REF_PATH, "mlkref_", True)
+        _ref = _Executor(REF_PATH, "mlkref_")
     return _ref
+
+
+def run_json(module, bufs, n: int, scalars=(), threads: int = 0):
+    """Runs an `mlk-kernel` module (dict or JSON text) through the compiled
+    reference's executeKernelOnBuffers, in place over f64 numpy buffers given
+    in table order (inputs, then outputs)."""
+    import json as _json
+
+    text = module if isinstance(module, str) else _json.dumps(module)
+    r = ref()
+    fn = r.lib.mlkref_run_json
+    fn.argtypes = [C.c_char_p, _vp, _i32, _i64, _vp, _i64, _i64]
+    for b in bufs:
+        assert b.dtype == np.float64 and b.flags["C_CONTIGUOUS"]
+    ptrs = (C.c_void_p * max(1, len(bufs)))(*[b.ctypes.data for b in bufs])
+    sc = np.ascontiguousarray(scalars, dtype=np.float64)
+    r._check(fn(text.encode(), ptrs, len(bufs), n, sc.ctypes.data if sc.size else None, sc.size,
+                threads))
+
+
+def pipeline_json(which: int, n: int, f32: bool = True):
+    """(module dict, patched constants) of a module the reference's own Tier-1
+    pipeline compiles: which 0 = sin(x*x + 3x) over a tensor x[n], 1 = its
+    Derivative through the reference's calculus passes, 2 = the scalar form."""
+    import json as _json
+
+    r = ref()
+    fn = r.lib.mlkref_pipeline_json
+    fn.argtypes = [_i32, _i64, _i32, C.c_char_p, _i64, C.POINTER(_i32)]
+    buf = C.create_string_buffer(1 << 16)
+    patched = _i32(0)
+    r._check(fn(which, n, int(f32), buf, 1 << 16, C.byref(patched)))
+    return _json.loads(buf.value.decode()), patched.value
 
 
 def best():

@@ -31,8 +31,10 @@ enum {
 /* KernelOperand::Kind, compiler/include/mlk/support/kernel_ir.h:59-67. */
 enum { K_CONST = 0, K_ELEM_A, K_ELEM_B, K_SCALAR, K_TEMP };
 
-/* ExprEvaluator::apply, kernel_buffers.cpp:130-159 (libm family). */
-static double apply_op(int op, double a, double b) {
+/* ExprEvaluator::apply, kernel_buffers.cpp:130-159; poly7 selects the
+ * "poly7" Sin family (resolveFamily, :42-51: Sin only). */
+static double poly7_sin(double x);
+static double apply_op(int op, double a, double b, int poly7) {
     switch (op) {
         case OP_ADD: return a + b;
         case OP_SUB: return a - b;
@@ -42,7 +44,7 @@ static double apply_op(int op, double a, double b) {
         case OP_POW: return (a == 2.0 && b == 2.0) ? a * a : pow(a, b);
         case OP_EXP: return exp(a);
         case OP_LOG: return a > 0.0 ? log(a) : 0.0;
-        case OP_SIN: return sin(a);
+        case OP_SIN: return poly7 ? poly7_sin(a) : sin(a);
         case OP_COS: return cos(a);
         case OP_TAN: return tan(a);
         case OP_TANH: return tanh(a);
@@ -53,6 +55,52 @@ static double apply_op(int op, double a, double b) {
             return 0.5 * a *
                    (1.0 + tanh(0.7978845608028654 * (a + 0.044715 * a * a * a)));
         default: return 0.0;
+    }
+}
+
+/* families::polySin, the "poly7" sine family
+ * (compiler/include/mlk/support/math_families.h:22-90): Cody-Waite quadrant
+ * reduction with pi/2 = hi + lo (:24-26, :69-76), then the degree-13 sine or
+ * degree-12 cosine residual polynomial (:30-65) picked by the quadrant
+ * (:81-90). Plain IEEE f64, no contraction (the oracle builds with
+ * -ffp-contract=off), in the reference's evaluation order. */
+static double poly7_sin_reduced(double x) {
+    const double r2 = x * x;
+    double p = 1.58962301576546568060e-10;
+    p = p * r2 + -2.50507477628578072866e-8;
+    p = p * r2 + 2.75573136213857245213e-6;
+    p = p * r2 + -1.98412698295895385996e-4;
+    p = p * r2 + 8.33333333332211858878e-3;
+    p = p * r2 + -1.66666666666666307295e-1;
+    return x + x * r2 * p;
+}
+
+static double poly7_cos_reduced(double x) {
+    const double r2 = x * x;
+    double p = -1.13585365213876817300e-11;
+    p = p * r2 + 2.08757530072652689750e-9;
+    p = p * r2 + -2.75573142103085808917e-7;
+    p = p * r2 + 2.48015872890001867312e-5;
+    p = p * r2 + -1.38888888888783992457e-3;
+    p = p * r2 + 4.16666666666666435770e-2;
+    return 1.0 - r2 * 0.5 + r2 * r2 * p;
+}
+
+static double poly7_sin(double x) {
+    const double n = floor(x / 1.57079632679489661923 + 0.5);
+    const double r = (x - n * 1.5707963267948965580e+00) - n * 6.1232339957367660359e-17;
+    /* For x NaN or infinite, fmod(n, 4) is NaN: the reference converts it to
+     * int, which x86-64 yields as INT_MIN, and its switch takes the default
+     * branch (-cos of a NaN residual). Take that branch without the
+     * undefined conversion, so even the NaN's sign matches. */
+    const double f = fmod(n, 4.0);
+    int q = isnan(f) ? 3 : (int)f;
+    if (q < 0) q += 4;
+    switch (q) {
+        case 0: return poly7_sin_reduced(r);
+        case 1: return poly7_cos_reduced(r);
+        case 2: return -poly7_sin_reduced(r);
+        default: return -poly7_cos_reduced(r);
     }
 }
 
@@ -83,8 +131,8 @@ static double eval_operand(int kind, int64_t index, double value,
 /* ExprEvaluator::run, kernel_buffers.cpp:161-178, driven per element by
  * runElementwiseRange (:342-402) over each top-level Loop (:921-953). */
 int mlko_chain(int32_t n_roots, const int32_t* root_len, const mlkb_expr* exprs,
-               const double* a, const double* b, double* const* outs, int64_t n,
-               const double* scalars, int64_t n_scalars) {
+               int32_t poly7, const double* a, const double* b, double* const* outs,
+               int64_t n, const double* scalars, int64_t n_scalars) {
     int32_t off = 0;
     for (int32_t r = 0; r < n_roots; ++r) {
         const mlkb_expr* ex = exprs + off;
@@ -104,7 +152,7 @@ int mlko_chain(int32_t n_roots, const int32_t* root_len, const mlkb_expr* exprs,
                         ? 0.0
                         : eval_operand(ex[k].b_kind, ex[k].b_index, ex[k].b_value,
                                        a, b, i, scalars, n_scalars, temps);
-                temps[k] = apply_op(ex[k].op, va, vb);
+                temps[k] = apply_op(ex[k].op, va, vb, poly7);
             }
             out[i] = (len - 1 < MAX_TEMPS) ? temps[len - 1] : 0.0;
         }

@@ -8,8 +8,8 @@
 extern "C" {
 #endif
 int mlko_chain(int32_t n_roots, const int32_t* root_len, const mlkb_expr* exprs,
-               const double* a, const double* b, double* const* outs, int64_t n,
-               const double* scalars, int64_t n_scalars);
+               int32_t poly7, const double* a, const double* b, double* const* outs,
+               int64_t n, const double* scalars, int64_t n_scalars);
 int mlko_softmax(const double* a, double* y, int64_t rows, int64_t cols);
 int mlko_reducesum(const double* a, double* y, int64_t rows, int64_t cols);
 int mlko_matmul_rows(const double* a, const double* b, double* c, int64_t n,

@@ -32,14 +32,14 @@ $(OUT)/libmlkref_core.a: $(OBJS)
 	ar rcs $@ $^
 
 # C-ABI driver over executeKernelOnBuffers (our code, reference headers).
-$(OUT)/libmlkref.so: oracle/ref_driver.cpp $(OUT)/libmlkref_core.a
+$(OUT)/libmlkref.so: oracle/ref_driver.cpp oracle/ref_modules.h $(OUT)/libmlkref_core.a
 	$(CXX) $(CXXFLAGS) $(INCS) -shared oracle/ref_driver.cpp \
 	  -Wl,--whole-archive $(OUT)/libmlkref_core.a -Wl,--no-whole-archive \
 	  -ldl -o $@
 
 # Drop-in check: the reference's own loadKernelLibrary + LoadedKernel::run
 # driving our mlk_kernel shim.
-$(OUT)/ref_loader_check: oracle/ref_loader_check.cpp $(OUT)/libmlkref_core.a
+$(OUT)/ref_loader_check: oracle/ref_loader_check.cpp oracle/ref_modules.h $(OUT)/libmlkref_core.a
 	$(CXX) $(CXXFLAGS) $(INCS) oracle/ref_loader_check.cpp \
 	  $(OUT)/libmlkref_core.a -ldl -o $@
 

@@ -16,6 +16,15 @@
 //     kernel_buffers.cpp:921-953);
 //   - Call(MatMul / Softmax / ReduceSum) over rank-2 buffers, the
 //     construction of tools/mlk-poly/poly_bench.cpp:123-160.
+// It also
+//   - reads any 1-D `mlk-kernel` JSON module back into the reference's
+//     KernelModule (the reference only writes the format, with
+//     KernelModule::toJson, compiler/src/support/kernel_ir.cpp:97-254), so
+//     the reference executor runs exactly the document the B200 path runs;
+//   - produces modules with the reference's OWN compiler: a GraphBuilder
+//     graph through PipelineRunner at Tier 1
+//     (compiler/src/pipeline/pipeline_runner.cpp:33-53), the way mlkc does
+//     (tools/mlkc/mlkc.cpp:117-150).
 #include <cstdint>
 #include <cstring>
 #include <string>
@@ -27,10 +36,13 @@
 #include "mlk/support/kernel_ir.h"
 
 #include "../include/mlkb200.h"
+#include "ref_modules.h"
 
 namespace {
 
-thread_local std::string g_err;
+using mlkb_oracle::g_err;
+using mlkb_oracle::loadModule;
+using mlkb_oracle::pipelineModule;
 
 int fail(const mlk::Error& e) {
     g_err = e.message;
@@ -241,6 +253,47 @@ int mlkref_module_json(int32_t kind, int32_t n_roots, const int32_t* root_len,
                            : kind == MLKB_KIND_MATMUL ? mlk::MathOp::MatMul
                                                       : mlk::MathOp::ReduceSum;
     return copyJson(buildCallModule(symbols, op, m, k, n, 0), symbols, buf, cap);
+}
+
+// Runs an `mlk-kernel` JSON module through executeKernelOnBuffers over f64
+// buffers given in table order (inputs, then outputs; temps are the
+// executor's own). n is KernelBufferBindings::elements.
+int mlkref_run_json(const char* json, double* const* bufs, int32_t n_bufs, int64_t n,
+                    const double* scalars, int64_t n_scalars, int64_t threads) {
+    mlk::SymbolTable symbols;
+    mlk::KernelModule km;
+    if (json == nullptr || !loadModule(json, symbols, km)) return 200;
+    if (threads > 0) *km.scheduleParams.findOrInsert(symbols.intern("threads"), nullptr) = threads;
+    mlk::KernelBufferBindings io;
+    int32_t k = 0;
+    for (const mlk::KernelBuffer& b : km.buffers) {
+        if (!b.isInput && !b.isOutput) continue;
+        if (k >= n_bufs) {
+            g_err = "fewer buffers than the module binds";
+            return 201;
+        }
+        (b.isInput ? io.inputs : io.outputs).push_back(bufs[k++]);
+    }
+    if (k != n_bufs) {
+        g_err = "more buffers than the module binds";
+        return 201;
+    }
+    for (int64_t i = 0; i < n_scalars; ++i) io.scalars.push_back(scalars[i]);
+    io.elements = n;
+    auto r = mlk::executeKernelOnBuffers(km, symbols, io, nullptr);
+    return r.has_value() ? 0 : fail(r.error());
+}
+
+// toJson of a module the reference's own pipeline compiles (pipelineModule
+// above); *patched counts the constants whose unset type was restored.
+int mlkref_pipeline_json(int32_t which, int64_t n, int32_t f32, char* buf, int64_t cap,
+                         int32_t* patched) {
+    mlk::SymbolTable symbols;
+    mlk::KernelModule km;
+    int p = 0;
+    if (!pipelineModule(which, n, f32 != 0, symbols, km, &p)) return 202;
+    if (patched != nullptr) *patched = p;
+    return copyJson(km, symbols, buf, cap);
 }
 
 }  // extern "C"

@@ -1,7 +1,7 @@
 // Drop-in check: drives the B200 shim through the REFERENCE's own artifact
 // loader, exactly as its fastkernel search and mlk-poly bench do.
 //
-// TEST INFRASTRUCTURE ONLY (run by tests/test_dropin.py on a GPU box).
+// TEST INFRASTRUCTURE ONLY (run by tests/test_dropin_gpu.py on a GPU box).
 //
 // For each module it
 //   1. builds the KernelModule with the reference's types,
@@ -26,6 +26,7 @@
 #include "mlk/runtime/execution.h"
 #include "mlk/support/json.h"
 #include "mlk/support/kernel_ir.h"
+#include "ref_modules.h"
 
 namespace {
 
@@ -73,7 +74,7 @@ void pushU(mlk::KernelNode& c) {
 }
 
 void addRoot(mlk::KernelModule& km, mlk::SymbolTable& sy, uint32_t in,
-             uint32_t out, bool deriv) {
+             uint32_t out, bool deriv, bool poly7 = false) {
     mlk::KernelNode loop;
     loop.op = mlk::KernelOp::Loop;
     loop.var = sy.intern(deriv ? "j" : "i");
@@ -90,6 +91,7 @@ void addRoot(mlk::KernelModule& km, mlk::SymbolTable& sy, uint32_t in,
         c.exprs.push_back(ex(mlk::MathOp::Mul, opnd(K::Temp, 0, 3), opnd(K::Temp, 0, 5)));
     }
     c.math = c.exprs[c.exprs.size() - 1].op;
+    if (poly7) c.family = sy.intern("poly7");
     mlk::KernelNode st;
     st.op = mlk::KernelOp::Store;
     st.bufferOut = out;
@@ -116,6 +118,7 @@ struct Case {
     std::vector<std::vector<double>> ins;
     std::vector<size_t> outSizes;
     int64_t elements;
+    std::vector<double> scalars = {};
 };
 
 int runCase(Case& c, mlk::SymbolTable& sy, const std::string& shim,
@@ -132,6 +135,7 @@ int runCase(Case& c, mlk::SymbolTable& sy, const std::string& shim,
         for (auto& v : c.ins) io.inputs.push_back(v.data());
         for (auto& v : outs) io.outputs.push_back(v.data());
         io.elements = c.elements;
+        for (double v : c.scalars) io.scalars.push_back(v);
         return io;
     };
     auto rr = mlk::executeKernelOnBuffers(c.km, sy, bindIo(ref), nullptr);
@@ -229,7 +233,84 @@ int main(int argc, char** argv) {
         (void)c.km.addNode(call);
         cases.push_back(std::move(c));
     }
+    {  // config-1 chain with the poly7 sine family (bit-exact bar)
+        Case c{"map_poly7", {}, {x}, {(size_t)n}, n};
+        const uint32_t in = c.km.addBuffer(buf(sy, "x", true, {}));
+        const uint32_t out = c.km.addBuffer(buf(sy, "y", false, {}));
+        addRoot(c.km, sy, in, out, false, true);
+        cases.push_back(std::move(c));
+    }
+    {  // the scaled-scores composite as the reference runs it: S += Q*Kt,
+       // Sc = S * 1/sqrt(d), Y = softmax(Sc), every intermediate an output
+        const int64_t s_ = 128, d = 64;
+        std::vector<double> q(s_ * d), kt(d * s_);
+        for (int64_t i = 0; i < s_ * d; ++i) q[i] = ((i * 37) % 23) * 0.125 - 1.375;
+        for (int64_t i = 0; i < d * s_; ++i) kt[i] = ((i * 11) % 17) * 0.0625 - 0.5;
+        Case c{"qk_composite", {}, {q, kt}, {(size_t)(s_ * s_), (size_t)(s_ * s_), (size_t)(s_ * s_)},
+               s_ * s_};
+        const uint32_t iq = c.km.addBuffer(buf(sy, "Q", true, {s_, d}));
+        const uint32_t ik = c.km.addBuffer(buf(sy, "Kt", true, {d, s_}));
+        const uint32_t is = c.km.addBuffer(buf(sy, "S", false, {s_, s_}));
+        const uint32_t isc = c.km.addBuffer(buf(sy, "Sc", false, {s_, s_}));
+        const uint32_t iy = c.km.addBuffer(buf(sy, "Y", false, {s_, s_}));
+        mlk::KernelNode mm;
+        mm.op = mlk::KernelOp::Call;
+        mm.math = mlk::MathOp::MatMul;
+        mm.bufferA = iq;
+        mm.bufferB = ik;
+        mm.bufferOut = is;
+        (void)c.km.addNode(mm);
+        mlk::KernelNode loop;
+        loop.op = mlk::KernelOp::Loop;
+        loop.var = sy.intern("i");
+        mlk::KernelNode comp;
+        comp.op = mlk::KernelOp::Compute;
+        comp.bufferA = is;
+        comp.exprs.push_back(ex(mlk::MathOp::Mul, opnd(K::ElemA), opnd(K::Const, 0.125)));
+        comp.math = mlk::MathOp::Mul;
+        mlk::KernelNode st;
+        st.op = mlk::KernelOp::Store;
+        st.bufferOut = isc;
+        const uint32_t l = c.km.addNode(loop);
+        const uint32_t ci = c.km.addNode(comp);
+        const uint32_t si = c.km.addNode(st);
+        c.km.nodes[l].children.push_back(ci);
+        c.km.nodes[l].children.push_back(si);
+        mlk::KernelNode sm;
+        sm.op = mlk::KernelOp::Call;
+        sm.math = mlk::MathOp::Softmax;
+        sm.bufferA = isc;
+        sm.bufferOut = iy;
+        (void)c.km.addNode(sm);
+        cases.push_back(std::move(c));
+    }
+    // Modules the reference's own Tier-1 pipeline compiles (ref_modules.h):
+    // sin(x^2+3x) over x[n], its derivative through the calculus passes, and
+    // the scalar form (x a ScalarParam). Each gets its own symbol table.
+    static mlk::SymbolTable psy[3];
+    for (int which = 0; which < 3; ++which) {
+        static const char* kNames[3] = {"pipeline_sin", "pipeline_dsin", "pipeline_scalar"};
+        const int64_t pn = which == 2 ? 1 : n;
+        Case c{kNames[which], {}, {}, {(size_t)pn}, pn};
+        int patched = 0;
+        if (!mlkb_oracle::pipelineModule(which, pn, false, psy[which], c.km, &patched)) {
+            std::printf("{\"case\":\"%s\",\"ok\":false,\"stage\":\"pipeline\",\"error\":\"%s\"}\n",
+                        kNames[which], mlkb_oracle::g_err.c_str());
+            return 1;
+        }
+        if (which == 2) {
+            c.scalars = {2.0};
+        } else {
+            c.ins = {x};
+        }
+        cases.push_back(std::move(c));
+    }
     int bad = 0;
-    for (Case& c : cases) bad += runCase(c, sy, shim, bind, status);
+    for (size_t i = 0; i < cases.size(); ++i) {
+        Case& c = cases[i];
+        const bool pipe = c.name.rfind("pipeline_", 0) == 0;
+        mlk::SymbolTable& table = pipe ? psy[c.name == "pipeline_sin" ? 0 : c.name == "pipeline_dsin" ? 1 : 2] : sy;
+        bad += runCase(c, table, shim, bind, status);
+    }
     return bad == 0 ? 0 : 1;
 }

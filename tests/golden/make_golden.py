@@ -13,7 +13,17 @@ results. Cases follow the reference's own tests where they exist:
     (inputs ((i*13)%19)*0.25-2, a NaN in row 9, -0/+0 ties in rows 10-11);
   * the K == 1 softmax shapes of unit_poly.cpp:3612-3650;
   * the GEMM operands of unit_poly.cpp:5150-5157 (A=(i%7)*0.25, B=(i%5)*0.5),
-    which the reference requires bit-exact.
+    which the reference requires bit-exact;
+  * the "poly7" sine family (compiler/include/mlk/support/math_families.h:
+    81-90) at its quadrant edges, the points its own certificate samples
+    (:113-137), and far outside them;
+  * modules the reference's OWN compiler produces (its Tier-1 pipeline over
+    sin(x^2+3x) and over its calculus passes' derivative of it), stored as
+    the JSON it wrote, with the reference executor's results on them;
+  * the scaled-scores composite Call(MatMul) -> scale map -> Call(Softmax) as
+    a module, with a nonzero initial S (MatMul accumulates into it).
+
+    python tests/golden/make_golden.py [section ...]   (default: all)
 """
 from __future__ import annotations
 
@@ -60,8 +70,85 @@ OP_CHAINS = {
 }
 
 
-def main() -> None:
+def main(sections) -> None:
     ref = oracle.ref()
+    if "base" in sections:
+        base(ref)
+    if "poly7" in sections:
+        poly7(ref)
+    if "pipeline" in sections:
+        pipeline()
+    if "qk" in sections:
+        qk()
+    print("golden vectors written to", HERE)
+
+
+def poly7(ref) -> None:
+    quarter = np.pi / 4
+    edges = np.array([k * quarter for k in range(-16, 17)] +
+                     [np.nextafter(k * quarter, np.inf) for k in range(-8, 9)] +
+                     [1e5, -1e5, 123456.789, 1e10, -3e15, 1e300, np.inf, -np.inf, np.nan,
+                      0.0, -0.0, 1e-300], np.float64)
+    sample = -np.pi + 2 * np.pi * np.arange(4096) / 4096  # the certificate's grid
+    x = np.concatenate([edges, sample, np.random.default_rng(11).uniform(-50, 50, 2048)])
+    with np.errstate(over="ignore"):
+        xf = x.astype(np.float32)  # the f32 path's inputs (out-of-range values become inf)
+    sin1 = chain(E("sin", A))
+    (y_sin,) = ref.chain([sin1], x, poly7=True)
+    (y_u,) = ref.chain([kir.SIN_CHAIN], xf.astype(np.float64), poly7=True)
+    (y_sinf,) = ref.chain([sin1], xf.astype(np.float64), poly7=True)
+    np.savez_compressed(os.path.join(HERE, "map_poly7.npz"), x=x, xf=xf, sin=y_sin,
+                        sin_u_f=y_u, sin_f=y_sinf, chain_sin=sin1, chain_u=kir.SIN_CHAIN)
+
+
+def pipeline() -> None:
+    import json
+
+    n = 4096
+    y_mod, _ = oracle.pipeline_json(0, n)
+    d_mod, patched = oracle.pipeline_json(1, n)
+    s_mod, _ = oracle.pipeline_json(2, 1)
+    both = kir.merge_roots([y_mod, d_mod], ["y", "dy"])
+    x = np.concatenate([EDGE, np.array([np.inf, -np.inf, np.nan, 1e30, -1e30], np.float32),
+                        oracle.fill_uniform_f32(n - EDGE.size - 5, SEED, 2, -8.0, 8.0)])
+    x64 = x.astype(np.float64)
+    y, dy = np.zeros(n), np.zeros(n)
+    oracle.run_json(both, [x64, y, dy], n)
+    ys, dys = np.zeros(n), np.zeros(n)
+    oracle.run_json(y_mod, [x64, ys], n)
+    oracle.run_json(d_mod, [x64, dys], n)
+    assert np.array_equal(ys.view(np.int64), y.view(np.int64))
+    assert np.array_equal(dys.view(np.int64), dy.view(np.int64), equal_nan=False) or \
+        np.array_equal(np.isnan(dys), np.isnan(dy))
+    xs = np.array([2.0, 0.0, -1.5, 3.0, 1e-3, -4.0])
+    s_out = []
+    for v in xs:
+        out = np.zeros(1)
+        oracle.run_json(s_mod, [out], 1, scalars=[v])
+        s_out.append(out[0])
+    np.savez_compressed(os.path.join(HERE, "pipeline.npz"),
+                        sin_json=json.dumps(y_mod), dsin_json=json.dumps(d_mod),
+                        both_json=json.dumps(both), scalar_json=json.dumps(s_mod),
+                        patched=patched, x=x, y=y, dy=dy, scalar_x=xs, scalar_y=np.array(s_out))
+
+
+def qk() -> None:
+    rng = np.random.default_rng(5)
+    s_, d_ = 128, 64
+    q = rng.normal(0, 1, (s_, d_)).astype(np.float16)
+    kt = np.ascontiguousarray(rng.normal(0, 1, (s_, d_)).astype(np.float16).T)
+    s0 = rng.normal(0, 2, (s_, s_)).astype(np.float32)  # MatMul accumulates into S
+    scale = d_ ** -0.5
+    mod = kir.qk_softmax_module(s_, d_, scale)
+    S, Sc, Y = s0.astype(np.float64), np.zeros((s_, s_)), np.zeros((s_, s_))
+    oracle.run_json(mod, [q.astype(np.float64), kt.astype(np.float64), S, Sc, Y], s_ * s_)
+    S0, Sc0, Y0 = np.zeros((s_, s_)), np.zeros((s_, s_)), np.zeros((s_, s_))
+    oracle.run_json(mod, [q.astype(np.float64), kt.astype(np.float64), S0, Sc0, Y0], s_ * s_)
+    np.savez_compressed(os.path.join(HERE, "qk.npz"), q=q, kt=kt, s0=s0, scale=scale,
+                        S=S, Sc=Sc, Y=Y, Y_zero=Y0)
+
+
+def base(ref) -> None:
     out = {}
 
     # config-1 chain: sin(x^2 + 3x), x ~ U(-4, 4), plus edge values
@@ -132,8 +219,7 @@ def main() -> None:
                         h_a=ha, h_b=hb, h_c0=hc,
                         h_c=ref.matmul(ha.astype(np.float64), hb.astype(np.float64),
                                        hc.astype(np.float64)))
-    print("golden vectors written to", HERE)
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:] or ["base", "poly7", "pipeline", "qk"])

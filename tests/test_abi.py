@@ -171,3 +171,79 @@ def test_no_device_is_reported_not_faked():
     with pytest.raises(mb.MLKBError):
         api.Module(kir.map_module([kir.SIN_CHAIN])).run_host(
             [x.astype(np.float32), y.astype(np.float32)], n=16)
+
+
+def _run_host_status(module, bufs, n):
+    ptrs = (C.c_void_p * len(bufs))(*[b.ctypes.data for b in bufs])
+    dts = (C.c_int32 * len(bufs))(*[api._dt_of(b) for b in bufs])
+    sc = (C.c_double * 1)(0.0)
+    return mb.lib().mlkb_module_run_host(module._h, ptrs, dts, len(bufs), n, sc, 0, 1)
+
+
+def test_qk_composite_forms():
+    # S and Sc outputs: the reference's three steps; temps: the fused kernel
+    out = api.Module(kir.qk_softmax_module(256, 64, 0.125))
+    assert out.kind == mb.KIND_QK_SOFTMAX and out.num_buffers == 5
+    assert out.plan([mb.F16, mb.F16, mb.F32, mb.F32, mb.F32]) == \
+        "gemm_f16_tcgen05,map_chain,softmax_f32"
+    assert out.plan([mb.F64] * 5) == "gemm_f64,map_chain,softmax_f64"
+    tmp = api.Module(kir.qk_softmax_module(256, 64, 0.125, temps=True))
+    assert tmp.kind == mb.KIND_QK_SOFTMAX and tmp.num_buffers == 3
+    assert tmp.plan([mb.F16, mb.F16, mb.F32]) == "qk_softmax_tcgen05_kt"
+    # one temp and one output intermediate: not a form this path runs
+    mixed = kir.qk_softmax_module(256, 64, 0.125)
+    mixed["buffers"][2]["output"] = False
+    mixed["buffers"][2]["temp"] = True
+    assert _status_of_create(kir.dumps(mixed)) == mb.ERR_UNSUPPORTED
+
+
+def test_qk_composite_run_requests_checked_before_any_device_work():
+    # These statuses come from the host-side checks, so they hold on a host
+    # without a GPU too: a run never returns OK for work it did not do.
+    s, d = 128, 64
+    q = np.zeros((s, d), np.float16)
+    kt = np.zeros((d, s), np.float16)
+    y = np.zeros((s, s), np.float32)
+    tmp = api.Module(kir.qk_softmax_module(s, d, 0.125, temps=True))
+    # temp scores need the scale map over all of S: n = s*s
+    assert _run_host_status(tmp, [q, kt, y], s * s - 1) == mb.ERR_UNSUPPORTED
+    # the fused form is f16 in, f32 out
+    assert _run_host_status(tmp, [q.astype(np.float64), kt.astype(np.float64),
+                                  y.astype(np.float64)], s * s) == mb.ERR_UNSUPPORTED
+    out = api.Module(kir.qk_softmax_module(s, d, 0.125))
+    sf = np.zeros((s, s), np.float32)
+    assert _run_host_status(out, [q, kt, sf, sf.astype(np.float64), y], s * s) == mb.ERR_INVALID
+    # a scale map running past S is the reference's out-of-range store
+    assert _run_host_status(out, [q, kt, sf, sf.copy(), y], s * s + 1) == mb.ERR_INVALID
+
+
+def test_failed_bind_leaves_nothing_bound():
+    # mlk_kernel must never run the previously bound module after a bind fails
+    L = mb.lib()
+    assert L.mlk_bind_module(kir.dumps(kir.map_module([kir.SIN_CHAIN], dtype="f64")).encode()) == 0
+    bad = kir.map_module([kir.SIN_CHAIN])
+    bad["nodes"][2]["accumulate"] = True
+    assert L.mlk_bind_module(kir.dumps(bad).encode()) == mb.ERR_UNSUPPORTED
+    x = np.zeros(4)
+    L.mlk_kernel(*([x.ctypes.data, x.ctypes.data, 4, 0, 0] + [0] * 13))
+    assert L.mlk_last_status() == mb.ERR_UNSUPPORTED
+    assert L.mlk_bind_module(None) == 0
+
+
+def test_mlk_kernel_rejects_a_negative_scalar_count():
+    # the reference reads any scalar index below the table size
+    # (kernel_buffers.cpp:114-117): tables of any size are accepted, a
+    # negative count is an error, and nothing is silently zeroed
+    L = mb.lib()
+    assert L.mlk_bind_module(kir.dumps(kir.map_module([kir.SIN_CHAIN], dtype="f64")).encode()) == 0
+    x, y = np.zeros(4), np.zeros(4)
+    sc = np.zeros(1)
+    L.mlk_kernel(*([x.ctypes.data, y.ctypes.data, 4, sc.ctypes.data, -1] + [0] * 13))
+    assert L.mlk_last_status() == mb.ERR_INVALID
+    assert L.mlk_bind_module(None) == 0
+
+
+def test_map_dtype_mismatch_checked_on_the_host():
+    m = api.Module(kir.map_module([kir.SIN_CHAIN]))
+    x = np.zeros(8, np.float32)
+    assert _run_host_status(m, [x, np.zeros(8, np.float64)], 8) == mb.ERR_INVALID

@@ -25,10 +25,19 @@ def test_reference_loader_runs_the_shim(cuda):
                          text=True, timeout=300)
     assert out.returncode == 0, out.stdout + out.stderr
     rows = {r["case"]: r for r in map(json.loads, out.stdout.strip().splitlines())}
-    assert set(rows) == {"map_sin", "map_sin_dsin", "softmax", "matmul"}
+    assert set(rows) == {"map_sin", "map_sin_dsin", "softmax", "matmul", "map_poly7",
+                         "qk_composite", "pipeline_sin", "pipeline_dsin", "pipeline_scalar"}
     for r in rows.values():
         assert r["ok"] and r["status"] == 0 and not r["multi_dim"], r
     assert rows["matmul"]["max_ulp_f64"] == 0          # bit-exact, as the reference demands
+    assert rows["map_poly7"]["max_ulp_f64"] == 0       # the poly7 family is restated exactly
     assert rows["map_sin"]["max_ulp_f64"] <= 4
     assert rows["map_sin_dsin"]["max_ulp_f64"] <= 8
     assert rows["softmax"]["max_ulp_f64"] <= 64
+    # S and Sc bit-exact (f64 GEMM in the reference's order, one multiply), Y
+    # through the f64 softmax
+    assert rows["qk_composite"]["max_ulp_f64"] <= 64
+    # modules compiled by the reference's own Tier-1 pipeline
+    assert rows["pipeline_sin"]["max_ulp_f64"] <= 4
+    assert rows["pipeline_dsin"]["max_ulp_f64"] <= 8
+    assert rows["pipeline_scalar"]["max_ulp_f64"] <= 4

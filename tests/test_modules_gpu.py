@@ -1,0 +1,132 @@
+"""Module-level paths on the GPU: the poly7 sine family, modules compiled by
+the reference's own pipeline, scalar tables of any size and roots with their
+own static ranges -- each against the reference's results.
+
+Bars: f32 maps <= 2 ULP of the f64 reference rounded to f32; the poly7 family
+bit-exact (it is restated in the same IEEE operations); f64 arithmetic
+bit-exact; f64 transcendentals <= 4 / 8 f64 ULP (CUDA vs glibc libm).
+"""
+import json
+
+import numpy as np
+import pytest
+
+import mlk2_b200 as mb
+import oracle
+from mlk2_b200 import api, kir
+from tests.gpu_util import dev, empty, host
+
+pytestmark = pytest.mark.gpu
+
+
+def same_bits(a, b):
+    return np.array_equal(np.asarray(a, np.float64).view(np.int64),
+                          np.asarray(b, np.float64).view(np.int64))
+
+
+def test_poly7_bit_exact(cuda, golden):
+    g = golden("map_poly7")
+    # f64 inputs, f64 outputs: bit for bit, NaN signs included
+    x = dev(cuda, g["x"])
+    y = empty(cuda, x.shape, cuda.float64)
+    api.map_chain(g["chain_sin"], x, y, poly7=True)
+    assert same_bits(host(y), g["sin"])
+    # f32 inputs: the same f64 value rounded once, so 0 ULP
+    xf = dev(cuda, g["xf"])
+    for ch, key in ((g["chain_sin"], "sin_f"), (g["chain_u"], "sin_u_f")):
+        yf = empty(cuda, xf.shape, cuda.float32)
+        api.map_chain(ch, xf, yf, poly7=True)
+        assert oracle.ulp_f32(host(yf), g[key]).max() == 0, key
+    # through a module (family="poly7" on the Compute node)
+    m = api.Module(kir.map_module([kir.SIN_CHAIN], poly7=True))
+    assert m.plan([mb.F32, mb.F32]) == "map_chain_poly7"
+    yf = empty(cuda, xf.shape, cuda.float32)
+    m.run_dev([xf, yf], n=xf.numel())
+    assert oracle.ulp_f32(host(yf), g["sin_u_f"]).max() == 0
+
+
+def test_poly7_reference_abi(cuda, golden):
+    g = golden("map_poly7")
+    x = np.ascontiguousarray(g["x"])
+    y = np.zeros_like(x)
+    assert api.legacy_call(kir.map_module([g["chain_sin"]], poly7=True, dtype="f64"),
+                           [x, y], x.size) == 0
+    assert same_bits(y, g["sin"])
+
+
+def _pipeline(golden):
+    g = golden("pipeline")
+    return g, {k: json.loads(str(g[k + "_json"])) for k in ("sin", "dsin", "both", "scalar")}
+
+
+def test_pipeline_modules_f32(cuda, golden):
+    # The reference's Tier-1 output for y and its calculus-pass derivative,
+    # as one two-root module: the dedicated fused kernel runs it.
+    g, m = _pipeline(golden)
+    both = api.Module(m["both"])
+    assert both.plan([mb.F32] * 3) == "map_sin_dsin_f32"
+    x = dev(cuda, g["x"])
+    y = empty(cuda, x.shape, cuda.float32)
+    dy = empty(cuda, x.shape, cuda.float32)
+    both.run_dev([x, y, dy], n=0)   # static bounds: n is not read
+    assert oracle.ulp_f32(host(y), g["y"]).max() <= 2
+    assert oracle.ulp_f32(host(dy), g["dy"]).max() <= 2
+    # host buffers, the caller's device and every visible device
+    for n_gpus in (1, 0):
+        yh, dyh = np.full(g["x"].size, np.nan, np.float32), np.full(g["x"].size, np.nan, np.float32)
+        both.run_host([g["x"], yh, dyh], n=0, n_gpus=n_gpus)
+        assert oracle.ulp_f32(yh, g["y"]).max() <= 2
+        assert oracle.ulp_f32(dyh, g["dy"]).max() <= 2
+    # the derivative on its own takes the generic chain, to the same bar
+    d = api.Module(m["dsin"])
+    dy2 = empty(cuda, x.shape, cuda.float32)
+    d.run_dev([x, dy2])
+    assert oracle.ulp_f32(host(dy2), g["dy"]).max() <= 2
+
+
+def test_pipeline_modules_reference_abi(cuda, golden):
+    g, m = _pipeline(golden)
+    x = g["x"].astype(np.float64)
+    y, dy = np.zeros_like(x), np.zeros_like(x)
+    assert api.legacy_call(m["both"], [x, y, dy], x.size) == 0
+    assert oracle.ulp_f64(y, g["y"]).max() <= 4
+    assert oracle.ulp_f64(dy, g["dy"]).max() <= 8
+    # the scalar form: x arrives as ScalarParam 0, one output element
+    for v, want in zip(g["scalar_x"], g["scalar_y"]):
+        out = np.zeros(1)
+        assert api.legacy_call(m["scalar"], [out], 1, scalars=[v]) == 0
+        assert oracle.ulp_f64(out, np.array([want])).max() <= 4
+
+
+def test_scalar_table_of_any_size(cuda):
+    # ScalarParam 100 of a 150-entry table, and 200 past its end (reads 0)
+    ch = kir.chain(kir.E("mul", kir.A, kir.S(100)), kir.E("add", kir.T(0), kir.S(5)),
+                   kir.E("add", kir.T(1), kir.S(200)))
+    scalars = np.arange(150, dtype=np.float64) * 0.75 - 3.0
+    xh = np.linspace(-5, 5, 1000)
+    x = dev(cuda, xh)
+    y = empty(cuda, x.shape, cuda.float64)
+    api.map_chain(ch, x, y, scalars=list(scalars))
+    (want,) = oracle.port().chain([ch], xh, scalars=scalars)
+    assert same_bits(host(y), want)
+    # and through the reference ABI, where the driver passes the whole table
+    yh = np.zeros_like(xh)
+    assert api.legacy_call(kir.map_module([ch], dtype="f64"), [xh.copy(), yh], xh.size,
+                           scalars=list(scalars)) == 0
+    assert same_bits(yh, want)
+
+
+def test_roots_with_their_own_static_ranges(cuda):
+    # root 0 stores [0, 1000) whatever n is; root 1 runs to the caller's n;
+    # each buffer is exactly as long as its root's range, so a copy past it
+    # would write outside the caller's array
+    mod = kir.map_module([kir.SIN_CHAIN, kir.chain(kir.E("mul", kir.A, kir.C(2.0)))])
+    mod["nodes"][0]["end"] = 1000
+    m = api.Module(mod)
+    xh = np.linspace(-3, 3, 1000).astype(np.float32)
+    y0 = np.full(1000, np.nan, np.float32)
+    y1 = np.full(500, np.nan, np.float32)
+    m.run_host([xh, y0, y1], n=500, n_gpus=1)
+    (r0,) = oracle.port().chain([kir.SIN_CHAIN], xh.astype(np.float64))
+    assert oracle.ulp_f32(y0, r0).max() <= 2
+    assert np.array_equal(y1, xh[:500] * 2)

@@ -130,3 +130,37 @@ def test_ulp_distance_rules():
     # across zero: smallest subnormals of opposite sign are 2 apart
     tiny = np.float32(1e-45)
     assert oracle.ulp_f32(tiny, -float(tiny))[()] == 2
+
+
+def test_golden_poly7(golden):
+    # the reference's "poly7" sine family (math_families.h:81-90), both on
+    # f64 inputs and on f32 inputs widened exactly
+    g = golden("map_poly7")
+    (y,) = port.chain([g["chain_sin"]], g["x"], poly7=True)
+    assert same_bits(y, g["sin"])
+    (y,) = port.chain([g["chain_sin"]], g["xf"].astype(np.float64), poly7=True)
+    assert same_bits(y, g["sin_f"])
+    (y,) = port.chain([g["chain_u"]], g["xf"].astype(np.float64), poly7=True)
+    assert same_bits(y, g["sin_u_f"])
+
+
+def test_poly7_is_a_different_family_within_its_certificate(golden):
+    # poly7 differs from libm somewhere on [-pi, pi], and by single-digit ULP
+    # at most there (the reference's own accuracy claim, math_families.h:10-13)
+    g = golden("map_poly7")
+    x = g["x"]
+    grid = (x >= -np.pi) & (x <= np.pi)
+    (p7,) = port.chain([g["chain_sin"]], x[grid], poly7=True)
+    (lm,) = port.chain([g["chain_sin"]], x[grid])
+    d = oracle.ulp_f64(p7, lm)
+    assert 0 < d.max() < 10
+    assert np.all(np.isnan(g["sin"][~np.isfinite(x)]))
+
+
+@needs_ref
+def test_poly7_port_matches_reference_fresh_inputs():
+    rng = np.random.default_rng(12)
+    x = np.concatenate([rng.uniform(-20, 20, 4000), rng.uniform(-1e6, 1e6, 1000)])
+    for chains in ([kir.chain(kir.E("sin", kir.A))], [kir.SIN_CHAIN, kir.DSIN_CHAIN]):
+        for a, b in zip(port.chain(chains, x, poly7=True), oracle.ref().chain(chains, x, poly7=True)):
+            assert same_bits(a, b)

@@ -70,3 +70,88 @@ def test_config5_full_size_sampled(cuda):
 def test_qk_module_composite_recognised():
     m = api.Module(kir.qk_softmax_module(2048, 128, 128 ** -0.5))
     assert m.kind == mb.KIND_QK_SOFTMAX
+
+
+# K given as the reference's MatMul B operand, Kt [batch, d, s], read in place
+# as the MN-major operand. (batch, m, s, d): m != s, the row-specialised
+# lengths, and shapes that take the two-step form (m or s not a multiple of
+# 128, d not in {64, 128}).
+@pytest.mark.parametrize("shape", [(2, 256, 256, 128), (1, 384, 512, 64), (3, 128, 1024, 64),
+                                   (1, 2048, 2048, 128), (2, 200, 136, 64), (1, 256, 200, 96)])
+def test_qk_softmax_kt(cuda, shape):
+    batch, m, s, d = shape
+    rng = np.random.default_rng(m + s + d)
+    q = rng.normal(0, 1, (batch, m, d)).astype(np.float16)
+    k = rng.normal(0, 1, (batch, s, d)).astype(np.float16)
+    kt = np.ascontiguousarray(k.transpose(0, 2, 1))
+    y = empty(cuda, (batch, m, s), cuda.float32)
+    api.qk_softmax_kt(dev(cuda, q), dev(cuda, kt), y, d ** -0.5)
+    check(host(y), reference(q, k, d ** -0.5))
+    assert api.take_device_error() == 0
+
+
+def test_qk_module_temp_form(cuda, golden):
+    # S and Sc temps: the fused kernel, Kt read in place. Its result is the
+    # reference's output form with S starting at zero.
+    g = golden("qk")
+    s_, d_ = g["q"].shape
+    mod = api.Module(kir.qk_softmax_module(s_, d_, float(g["scale"]), temps=True))
+    assert mod.plan([mb.F16, mb.F16, mb.F32]) == "qk_softmax_tcgen05_kt"
+    y = empty(cuda, (s_, s_), cuda.float32)
+    mod.run_dev([dev(cuda, g["q"]), dev(cuda, g["kt"]), y], n=s_ * s_)
+    check(host(y), g["Y_zero"])
+    yh = np.full((s_, s_), np.nan, np.float32)
+    mod.run_host([g["q"], g["kt"], yh], n=s_ * s_, n_gpus=1)
+    check(yh, g["Y_zero"])
+    assert api.take_device_error() == 0
+
+
+def test_qk_module_temp_form_full_rows(cuda):
+    # one config-5 batch through the module, every row sum 1, sampled rows
+    # against the oracle; on several GPUs the rows are split in 128-row bands
+    s_, d_ = 2048, 128
+    rng = np.random.default_rng(9)
+    q = rng.normal(0, 1, (s_, d_)).astype(np.float16)
+    k = rng.normal(0, 1, (s_, d_)).astype(np.float16)
+    kt = np.ascontiguousarray(k.T)
+    mod = api.Module(kir.qk_softmax_module(s_, d_, d_ ** -0.5, temps=True))
+    yh = np.full((s_, s_), np.nan, np.float32)
+    mod.run_host([q, kt, yh], n=s_ * s_, n_gpus=0)
+    assert np.abs(yh.astype(np.float64).sum(axis=1) - 1).max() < 1e-4
+    rows = np.array([0, 1, 127, 128, 1023, 1024, 2047])
+    o = oracle.port()
+    sc = o.matmul(q[rows].astype(np.float64), kt.astype(np.float64)) * d_ ** -0.5
+    check(yh[rows], o.softmax(sc))
+
+
+@pytest.mark.parametrize("dtype", ["f16", "f32"])
+def test_qk_module_output_form(cuda, golden, dtype):
+    # S and Sc outputs: S += Q*Kt (S starts from the caller's values),
+    # Sc = S*scale, Y = softmax(Sc) -- the reference's three steps on the GPU
+    g = golden("qk")
+    s_, d_ = g["q"].shape
+    mod = api.Module(kir.qk_softmax_module(s_, d_, float(g["scale"]), dtype=dtype))
+    npdt = np.float16 if dtype == "f16" else np.float32
+    S = g["s0"].copy()
+    Sc = np.full_like(S, np.nan)
+    Y = np.full_like(S, np.nan)
+    mod.run_host([g["q"].astype(npdt), g["kt"].astype(npdt), S, Sc, Y], n=s_ * s_, n_gpus=1)
+    # f32 accumulation of f16 products onto S: componentwise bound
+    q64, kt64 = g["q"].astype(np.float64), g["kt"].astype(np.float64)
+    bound = 2.0**-12 * (np.abs(q64) @ np.abs(kt64) + np.abs(g["s0"]))
+    assert np.all(np.abs(S - g["S"]) <= bound)
+    assert np.all(Sc == (S.astype(np.float64) * float(g["scale"])).astype(np.float32))
+    check(Y, g["Y"])
+
+
+def test_qk_module_output_form_reference_abi(cuda, golden):
+    # f64 through the reference's legacy mlk_kernel call: S and Sc bit-exact
+    g = golden("qk")
+    s_, d_ = g["q"].shape
+    mod = kir.qk_softmax_module(s_, d_, float(g["scale"]), dtype="f64")
+    S = g["s0"].astype(np.float64)
+    Sc, Y = np.zeros_like(S), np.zeros_like(S)
+    assert api.legacy_call(mod, [g["q"].astype(np.float64), g["kt"].astype(np.float64), S, Sc, Y],
+                           s_ * s_) == 0
+    assert np.array_equal(S, g["S"]) and np.array_equal(Sc, g["Sc"])
+    assert oracle.ulp_f64(Y, g["Y"]).max() <= 64

@@ -14,8 +14,21 @@ Timing: W warm-up steps, then K steps bracketed by a barrier and a device
 synchronise, CUDA events on the launching stream, max over ranks. Inputs
 (1 GiB per shard) exceed the 126 MB L2, so no flush is needed. nvidia-smi
 clocks are sampled during the timed region. `e2e` is the same metric through
-the C-ABI host entry (mlkb_module_run_host) from pinned host buffers, with
-the H2D copy of x and the D2H copy of y and dy inside every step.
+the C-ABI host entry (mlkb_module_run_host) on the module the reference's own
+compiler emits for config 2 (its Tier-1 pipeline output for y and for the
+calculus passes' dy, committed in tests/golden/pipeline.npz, at 2^28
+elements), from pinned host buffers, with the H2D copy of x and the D2H copy
+of y and dy inside every one of the K steps.
+
+With N > 1 ranks a strong-scaling pass follows: each fixed BASELINE problem
+(2^24 / 2^28 elements, 65536 rows, M = 8192, 256 batches) is split over the
+N ranks and timed the same way, plus the NCCL all-gather that assembles the
+config-2 result.
+
+The line is kept short (the full record goes to --detail PATH): the driver
+keeps the end of stdout, so `configs` and `strong` come last, in short keys:
+v = value, u = unit, ms = ms per step, f = roofline fraction (burst, of the
+measured peak), fs = the same after 1.5 s of continuous running, ok = parity.
 
 --impl reference times the reference's own CPU executor (oracle/_ref, built
 from the reference sources; the C restatement when absent) on rank 0 with
@@ -329,6 +342,8 @@ def main():
     ap.add_argument("--case", default=None,
                     choices=["map1", "map2", "softmax", "gemm", "gemm_f32", "qk"],
                     help="run one kernel W+K times (profiling target), no JSON line")
+    ap.add_argument("--detail", default=None,
+                    help="also write the full (verbose) record as JSON to this path")
     ap.add_argument("--size", type=int, default=0,
                     help="--case size: elements (maps), rows (softmax), M=N=K (gemm), batch (qk)")
     args = ap.parse_args()
@@ -410,17 +425,31 @@ def main():
         torch.cuda.empty_cache()
 
     # ---- e2e through the C-ABI host entry ---------------------------------------
+    # The module is the reference compiler's own output for config 2 (Tier-1
+    # pipeline, y and the calculus passes' dy), stretched to 2^28 elements.
     del y, dy
+    import numpy as _np
+
+    pipe = _np.load(os.path.join(ROOT, "tests", "golden", "pipeline.npz"))
+    module_doc = kir.with_static_length(json.loads(str(pipe["both_json"])), n)
+    module = api.Module(module_doc)
+    plan = module.plan([mb.F32] * 3)
+    # device-timed run of the same module through mlkb_module_run_dev
+    ym, dym = torch.empty_like(x), torch.empty_like(x)
+    msec = time_device(torch, lambda: module.run_dev([x, ym, dym], n=n), args.warmup,
+                       args.steps, dist, world)
+    module_dev = {"plan": plan, "ms": msec * 1e3,
+                  "f": alg_bytes / msec / 1e9 / peaks["hbm_gbs"]}
+    del ym, dym
     xh = torch.empty(n, dtype=torch.float32).pin_memory()
     yh = torch.empty(n, dtype=torch.float32).pin_memory()
     dyh = torch.empty(n, dtype=torch.float32).pin_memory()
     xh.copy_(x.cpu())
     del x
     torch.cuda.empty_cache()
-    module = api.Module(kir.map_module([kir.SIN_CHAIN, kir.DSIN_CHAIN]))
     bufs = [xh, yh, dyh]
     module.run_host(bufs, n=n, n_gpus=1)  # warm the device buffer cache
-    e2e_steps = max(2, min(args.steps, 5))
+    e2e_steps = args.steps
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
@@ -431,9 +460,10 @@ def main():
         t = torch.tensor([e2e_sec], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_sec = float(t.item())
-    e2e = {"value": world * alg_bytes / e2e_sec / 1e9, "unit": "GB/s",
+    e2e = {"value": round(world * alg_bytes / e2e_sec / 1e9, 2), "unit": "GB/s",
            "h2d_bytes_per_step": n * 4, "d2h_bytes_per_step": n * 8,
-           "ms_per_step": e2e_sec * 1e3, "api": "mlkb_module_run_host (pinned host f32)"}
+           "ms_per_step": round(e2e_sec * 1e3, 3), "steps": e2e_steps,
+           "api": "mlkb_module_run_host, reference-compiled module, pinned host f32"}
     del xh, yh, dyh, bufs, module
     torch.cuda.empty_cache()
 
@@ -442,43 +472,159 @@ def main():
     if not args.headline_only:
         configs = other_configs(torch, api, args, dist, world, rank, peaks, traffic)
 
+    # ---- strong scaling: each fixed problem split over the ranks -------------------
+    strong = None
+    if world > 1 and not args.headline_only:
+        strong = strong_configs(torch, api, mdist, args, dist, world, rank, peaks)
+
     # ---- CPU baseline (rank 0, N = 1 only) ----------------------------------------
     cpu = None
     if rank == 0 and world == 1:
         v, kind, cores, t = cpu_reference_map2(1 << 24, 3)
-        cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind,
-               "sample": "2^24 elements of config 2 per run (median of 3), f64 arithmetic, "
-                         "bytes counted at f32 width (12 B/element)"}
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+               "sample": "2^24 of the 2^28 config-2 elements, f64, bytes at f32 width"}
         if kind == "reference":
             vd, _, cd, _ = cpu_reference_map2(1 << 24, 3, default_threads=True)
-            cpu["default_executor"] = {"value": vd, "cores": cd,
-                                       "note": "the executor's default schedule (<= 4 threads)"}
+            cpu["default_executor"] = {"value": round(vd, 3), "cores": cd}
         if configs:
             for name, base in cpu_reference_configs().items():
                 if name in configs:
                     configs[name]["cpu_baseline"] = base
 
     if rank == 0:
+        launches = args.steps * 2 + sum(c.get("gpu_launches", 0) for c in configs.values())
+        if strong:
+            launches += sum(c.get("gpu_launches", 0) for c in strong.values() if isinstance(c, dict))
+        detail = {
+            "metric": "HBM GB/s (map/softmax) & GEMM TFLOP/s vs B200 peak at 1/2/4/8 GPUs",
+            "value": value, "roofline": roofline, "parity": gate, "cpu_baseline": cpu,
+            "e2e": e2e, "gather": gather, "module_dev": module_dev, "clocks": clocks,
+            "step_ms": step_ms, "configs": configs, "strong": strong, "library": mb.version(),
+        }
+        if args.detail:
+            with open(args.detail, "w") as f:
+                json.dump(detail, f, indent=1)
+
+        def r(v, k=4):
+            return None if v is None else float(f"{v:.{k}g}")
+
+        def short(c):
+            d = {"v": r(c["value"]), "u": c["unit"], "ms": r(c["ms_per_step"]),
+                 "f": r(c["roofline"]["frac"], 3)}
+            if "sustained" in c:
+                d["fs"] = r(c["sustained"]["frac"], 3)
+            if "parity" in c:
+                d["ok"] = bool(c["parity"]["pass"])
+            if c.get("cpu_baseline"):
+                d["cpu"] = r(c["cpu_baseline"]["value"], 3)
+            return d
+
         line = {
             "metric": "HBM GB/s (map/softmax) & GEMM TFLOP/s vs B200 peak at 1/2/4/8 GPUs",
-            "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "value": r(value, 6), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r(sec * 1e3, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded SplitMix64 U(-8,8), generated on the device)",
-            "config": {"workload": "config2: y=sin(x^2+3x) and dy/dx=cos(x^2+3x)(2x+3), one "
-                                   "fused kernel, f32 in/out, f64 arithmetic",
-                       "elements_per_gpu": n, "global_elements": n * world,
-                       "parallelism": f"dp{world} (contiguous element shards)",
-                       "l2": "inputs 1 GiB per GPU > 126 MB L2, no flush"},
-            "roofline": roofline, "parity": gate, "cpu_baseline": cpu, "e2e": e2e,
-            "gather": gather,
-            "gpu_launches": args.steps + sum(c.get("gpu_launches", 0) for c in configs.values()),
-            "clocks": clocks, "step_ms": step_ms, "configs": configs, "library": mb.version(),
+            "data": "synthetic, seeded U(-8,8), generated on the device",
+            "config": {"workload": "config2 y=sin(x^2+3x), dy=cos(x^2+3x)(2x+3), f32, "
+                                   "one fused kernel", "elements_per_gpu": n,
+                       "parallelism": f"dp{world}", "l2": "1 GiB inputs > L2, no flush"},
+            "roofline": {"bound": "hbm", "achieved": r(achieved, 5), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": r(roofline["frac"], 4),
+                         "traffic": roofline["traffic"]},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+            "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"],
+                       "reasons": clocks["reasons"]},
+            "parity_ok": bool(gate["y"]["pass"] and gate["dy"]["pass"]),
+            "module": {"plan": module_dev["plan"], "ms": r(module_dev["ms"]),
+                       "f": r(module_dev["f"], 3)},
         }
-        print(json.dumps(line), flush=True)
+        if gather is not None:
+            line["gather"] = {"ms": r(gather["ms"]), "busbw": r(gather["busbw_gbs"])}
+        line["configs"] = {k: short(c) for k, c in configs.items()}
+        if strong:
+            line["strong"] = {k: ({"v": r(c["value"]), "ms": r(c["ms"]), "f": r(c["frac"], 3)}
+                                  if "value" in c else {"ms": r(c["ms"]), "busbw": r(c["busbw"])})
+                              for k, c in strong.items()}
+        print(json.dumps(line, separators=(",", ":")), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def strong_configs(torch, api, mdist, args, dist, world, rank, peaks):
+    """Each fixed BASELINE problem split over the ranks (contiguous element,
+    row, M-block and batch shards; B replicated for the GEMM). value = the
+    whole problem's work / the slowest rank's step time."""
+    out = {}
+    hbm, tc = peaks["hbm_gbs"], peaks["bf16_tflops"]
+
+    def rec(name, fn, work, unit, peak):
+        sec = time_device(torch, fn, args.warmup, args.steps, dist, world)
+        scale = 1e9 if unit == "GB/s" else 1e12
+        out[name] = {"value": work / sec / scale, "unit": unit, "ms": sec * 1e3,
+                     "frac": work / sec / scale / (world * peak), "gpu_launches": args.steps}
+
+    def part(total):
+        return total * (rank + 1) // world - total * rank // world
+
+    # config 1 (2^24) and config 2 (2^28) element shards
+    n1 = part(1 << 24)
+    x1 = torch.empty(n1, device="cuda")
+    api.fill(x1, SEED, 1 + 256 * rank, "uniform", -4.0, 4.0)
+    y1 = torch.empty_like(x1)
+    rec("map1", lambda: api.map_sin(x1, y1), (1 << 24) * 8, "GB/s", hbm)
+    del x1, y1
+    n2 = part(1 << 28)
+    x2 = torch.empty(n2, device="cuda")
+    api.fill(x2, SEED, 2 + 256 * rank, "uniform", -8.0, 8.0)
+    y2, dy2 = torch.empty_like(x2), torch.empty_like(x2)
+    rec("map2", lambda: api.map_sin_dsin(x2, y2, dy2), (1 << 28) * 12, "GB/s", hbm)
+    # assembling y on every rank: NCCL all-gather (the only collective)
+    if (1 << 28) % world == 0:
+        for _ in range(2):
+            del_full = mdist.all_gather_shards(y2, dist)
+            del del_full
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        full = mdist.all_gather_shards(y2, dist)
+        g1.record()
+        torch.cuda.synchronize()
+        gms = mdist.max_over_ranks(g0.elapsed_time(g1), dist, device="cuda")
+        nbytes = full.numel() * 4
+        out["gather_map2_y"] = {"ms": gms, "busbw": nbytes * (world - 1) / world / (gms / 1e3) / 1e9}
+        del full
+    del x2, y2, dy2
+    torch.cuda.empty_cache()
+    # config 3: row shards of 65536 x 4096
+    r3 = part(65536)
+    xs = torch.empty((r3, 4096), device="cuda")
+    api.fill(xs, SEED, 3 + 256 * rank, "normal", 0.0, 4.0)
+    ys = torch.empty_like(xs)
+    rec("softmax", lambda: api.softmax(xs, ys), 2 * 4 * 65536 * 4096, "GB/s", hbm)
+    del xs, ys
+    # config 4: M-block shards of the 8192^3 GEMM, B on every rank
+    m4 = part(8192)
+    a = torch.empty((m4, 8192), dtype=torch.float16, device="cuda")
+    b = torch.empty((8192, 8192), dtype=torch.float16, device="cuda")
+    api.fill(a, SEED, 41 + 256 * rank, "normal", 0.0, 8192 ** -0.5)
+    api.fill(b, SEED, 42, "normal", 0.0, 8192 ** -0.5)
+    c = torch.empty((m4, 8192), device="cuda")
+    rec("gemm_f16", lambda: api.gemm(a, b, c), 2.0 * 8192 ** 3, "TFLOP/s", tc)
+    del a, b, c
+    # config 5: batch shards of 256 x [2048 x 2048]
+    bq = part(256)
+    q = torch.empty((bq, 2048, 128), dtype=torch.float16, device="cuda")
+    k = torch.empty((bq, 2048, 128), dtype=torch.float16, device="cuda")
+    api.fill(q, SEED, 51 + 256 * rank, "normal", 0.0, 1.0)
+    api.fill(k, SEED, 52 + 256 * rank, "normal", 0.0, 1.0)
+    yq = torch.empty((bq, 2048, 2048), device="cuda")
+    rec("qk_softmax", lambda: api.qk_softmax(q, k, yq, 128 ** -0.5),
+        2 * 256 * 2048 * 128 * 2 + 256 * 2048 * 2048 * 4, "GB/s", hbm)
+    del q, k, yq
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_case(args):

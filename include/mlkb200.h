@@ -207,6 +207,34 @@ int mlkb_module_run_host(const mlkb_module* module, void* const* bufs,
                          const double* scalars, int64_t n_scalars,
                          int32_t n_gpus);
 
+/* Flag of mlkb_module_run_sharded: assemble every output on device 0. */
+#define MLKB_ASSEMBLE_DEVICE0 1u
+
+/*
+ * The typed multi-GPU entry: runs the module sharded over devices
+ * 0..n_gpus-1 (n_gpus <= 0: all visible devices) in contiguous element / row
+ * / batch shards, inputs read from HOST buffers.
+ *   flags 0                       outputs are host buffers: mlkb_module_run_host.
+ *   flags MLKB_ASSEMBLE_DEVICE0   output buffers are DEVICE memory on device 0;
+ *                                 each shard's part of every output is
+ *                                 assembled there by grouped NCCL send/recv
+ *                                 over NVLink (no kernel reads a peer's
+ *                                 memory). Outputs a step reads back (MatMul's
+ *                                 C, the composite's S, map outputs written in
+ *                                 part) are first sent from device 0 to the
+ *                                 shards the same way.
+ * NCCL is loaded on first use (libnccl.so.2, or the library named by the
+ * environment variable MLKB_NCCL_LIB) and one communicator per device is kept
+ * for the process; loading, communicator creation or a transfer failing
+ * returns MLKB_ERR_NCCL. Synchronous. No reference counterpart: the reference's
+ * artifact ABI is single-device (reference docs/kernel_abi.md:20-41); this is
+ * the typed extension its driver would bind for n GPUs with a gather flag.
+ */
+int mlkb_module_run_sharded(const mlkb_module* module, void* const* bufs,
+                            const int32_t* dtypes, int32_t n_bufs, int64_t n,
+                            const double* scalars, int64_t n_scalars, int32_t n_gpus,
+                            uint32_t flags);
+
 /* ======================================================================= */
 /* 3. Direct kernel entry points (device pointers, asynchronous on stream)  */
 /* ======================================================================= */

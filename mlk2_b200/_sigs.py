@@ -23,6 +23,7 @@ SIGNATURES = {
     "mlkb_module_plan": (i32, [vp, C.POINTER(i32), i32, C.c_char_p, i64]),
     "mlkb_module_run_dev": (i32, [vp, C.POINTER(vp), C.POINTER(i32), i32, i64, C.POINTER(f64), i64, i32, vp]),
     "mlkb_module_run_host": (i32, [vp, C.POINTER(vp), C.POINTER(i32), i32, i64, C.POINTER(f64), i64, i32]),
+    "mlkb_module_run_sharded": (i32, [vp, C.POINTER(vp), C.POINTER(i32), i32, i64, C.POINTER(f64), i64, i32, u32]),
     "mlkb_map_sin_f32": (i32, [vp, vp, i64, vp]),
     "mlkb_map_sin_dsin_f32": (i32, [vp, vp, vp, i64, vp]),
     "mlkb_map_chain": (i32, [vp, i32, i32, vp, vp, vp, i32, i64, C.POINTER(f64), i64, vp]),

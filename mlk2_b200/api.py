@@ -13,6 +13,8 @@ import numpy as np
 
 from . import F16, F32, F64, check, kir, lib
 
+ASSEMBLE_DEVICE0 = 1  # MLKB_ASSEMBLE_DEVICE0
+
 _TORCH_DT = None
 
 
@@ -171,6 +173,15 @@ class Module:
     def run_host(self, bufs, n: int = 0, scalars: Sequence[float] = (), n_gpus: int = 0):
         ptrs, dts, nb, sc = self._args(bufs, scalars)
         check(lib().mlkb_module_run_host(self._h, ptrs, dts, nb, n, sc, len(scalars), n_gpus))
+
+    def run_sharded(self, bufs, n: int = 0, scalars: Sequence[float] = (), n_gpus: int = 0,
+                    assemble: bool = True) -> int:
+        """Inputs from host buffers, sharded over n_gpus devices; with
+        `assemble` the outputs are device-0 tensors filled by NCCL. Returns
+        the status (0 = ok) rather than raising, for fault-injection tests."""
+        ptrs, dts, nb, sc = self._args(bufs, scalars)
+        return lib().mlkb_module_run_sharded(self._h, ptrs, dts, nb, n, sc, len(scalars), n_gpus,
+                                             ASSEMBLE_DEVICE0 if assemble else 0)
 
 
 def legacy_call(module: dict, host_f64: Sequence[np.ndarray], n: int,

@@ -10,8 +10,10 @@
 //   * the module bound once from its wire format instead of baked into
 //     generated source.
 #include <dlfcn.h>
+#include <nccl.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -785,6 +787,281 @@ int runHost(const Module& m, void* const* bufs, const int32_t* dt, int32_t n_buf
     return okStatus();
 }
 
+// ---- sharded runs assembled on device 0 (NCCL) ----------------------------------
+// The caller's inputs are host buffers; every device computes its contiguous
+// shard, and each output is assembled in the caller's buffer on device 0 by
+// NCCL point-to-point transfers over NVLink, grouped so all shards move at
+// once (no kernel of this library reads another GPU's memory). Outputs a step
+// reads back (MatMul's C, the composite's S, a map output written only in
+// part) are first scattered from device 0 the same way.
+
+// NCCL, loaded on first use: libnccl.so.2, or the library MLKB_NCCL_LIB names.
+struct NcclApi {
+    bool ok = false;
+    std::string path, err;
+    ncclResult_t (*commInitAll)(ncclComm_t*, int, const int*) = nullptr;
+    ncclResult_t (*groupStart)() = nullptr;
+    ncclResult_t (*groupEnd)() = nullptr;
+    ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*errorString)(ncclResult_t) = nullptr;
+};
+
+std::mutex g_ncclMu;               // guards the two caches below and every assembled run
+std::vector<NcclApi> g_nccl;       // one entry per library path tried
+std::vector<std::pair<std::string, std::vector<ncclComm_t>>> g_cliques;  // (path#g, comms)
+
+const NcclApi& ncclApi() {
+    const char* env = std::getenv("MLKB_NCCL_LIB");
+    const std::string path = (env != nullptr && *env != '\0') ? env : "libnccl.so.2";
+    for (const NcclApi& a : g_nccl) {
+        if (a.path == path) return a;
+    }
+    NcclApi a;
+    a.path = path;
+    void* h = dlopen(path.c_str(), RTLD_NOW | RTLD_LOCAL);
+    if (h == nullptr) {
+        const char* e = dlerror();
+        a.err = std::string("cannot load ") + path + ": " + (e != nullptr ? e : "?");
+    } else {
+        a.commInitAll = reinterpret_cast<decltype(a.commInitAll)>(dlsym(h, "ncclCommInitAll"));
+        a.groupStart = reinterpret_cast<decltype(a.groupStart)>(dlsym(h, "ncclGroupStart"));
+        a.groupEnd = reinterpret_cast<decltype(a.groupEnd)>(dlsym(h, "ncclGroupEnd"));
+        a.send = reinterpret_cast<decltype(a.send)>(dlsym(h, "ncclSend"));
+        a.recv = reinterpret_cast<decltype(a.recv)>(dlsym(h, "ncclRecv"));
+        a.errorString = reinterpret_cast<decltype(a.errorString)>(dlsym(h, "ncclGetErrorString"));
+        a.ok = a.commInitAll && a.groupStart && a.groupEnd && a.send && a.recv && a.errorString;
+        if (!a.ok) a.err = path + " lacks the NCCL entry points this path uses";
+    }
+    g_nccl.push_back(a);
+    return g_nccl.back();
+}
+
+int ncclFail(const NcclApi& api, ncclResult_t r, const char* what) {
+    return setError(MLKB_ERR_NCCL, (std::string(what) + ": " + api.errorString(r)).c_str());
+}
+
+// One communicator per device 0..g-1, created once per library and device count.
+int ncclClique(const NcclApi& api, int g, std::vector<ncclComm_t>** out) {
+    const std::string key = api.path + "#" + std::to_string(g);
+    for (auto& c : g_cliques) {
+        if (c.first == key) {
+            *out = &c.second;
+            return okStatus();
+        }
+    }
+    std::vector<ncclComm_t> comms(static_cast<size_t>(g), nullptr);
+    std::vector<int> devs(static_cast<size_t>(g));
+    for (int d = 0; d < g; ++d) devs[static_cast<size_t>(d)] = d;
+    const ncclResult_t r = api.commInitAll(comms.data(), g, devs.data());
+    if (r != ncclSuccess) return ncclFail(api, r, "ncclCommInitAll");
+    g_cliques.emplace_back(key, std::move(comms));
+    *out = &g_cliques.back().second;
+    return okStatus();
+}
+
+// What one shard moves and runs: per bindable buffer, the element range it
+// covers, whether it is staged from the host (inputs), brought from device 0
+// first (outputs a step reads back) or assembled on device 0 afterwards.
+struct BufPlan {
+    int64_t off = 0, cnt = 0;
+    bool in = false, rmw = false, out = false;
+    void* slot = nullptr;
+};
+
+struct ShardPlan {
+    int dev = 0;
+    Module m;
+    std::vector<BufPlan> b;
+    cudaStream_t st = nullptr;
+};
+
+ShardPlan planShard(const Module& m0, const Shard& sh, int64_t n) {
+    ShardPlan p;
+    p.dev = sh.dev;
+    p.m = m0;
+    const size_t nb = m0.bindable.size();
+    p.b.resize(nb);
+    const int64_t units = sh.u1 - sh.u0;
+    if (m0.kind == MLKB_KIND_MAP) {
+        std::vector<int64_t> ext(nb, 0);
+        for (const MapRoot& r : m0.roots) {
+            const int64_t rEnd = r.end < 0 ? n : r.end;
+            for (size_t i = 0; i < nb; ++i) {
+                const int bid = m0.bindable[i];
+                if ((bid == r.out || bid == r.a || bid == r.b) && rEnd > ext[i]) ext[i] = rEnd;
+            }
+        }
+        for (size_t i = 0; i < nb; ++i) {
+            const int64_t v = ext[i] - sh.u0;
+            p.b[i].off = sh.u0;
+            p.b[i].cnt = v <= 0 ? 0 : (v < units ? v : units);
+            p.b[i].in = m0.buffers[m0.bindable[i]].input;
+        }
+        for (MapRoot& r : p.m.roots) {
+            const int64_t rEnd = r.end < 0 ? n : r.end;
+            const int64_t lo = r.begin > sh.u0 ? r.begin : sh.u0;
+            const int64_t hi = rEnd < sh.u1 ? rEnd : sh.u1;
+            r.begin = lo - sh.u0;
+            r.end = hi > lo ? hi - sh.u0 : r.begin;
+            if (hi <= lo) continue;
+            for (size_t i = 0; i < nb; ++i) {
+                if (m0.bindable[i] != r.out) continue;
+                p.b[i].out = true;
+                if (lo != sh.u0 || hi != sh.u0 + p.b[i].cnt) p.b[i].rmw = true;
+            }
+        }
+        return p;
+    }
+    p.m.m = units;
+    const bool qk = m0.kind == MLKB_KIND_QK_SOFTMAX;
+    bool scPartial = false;
+    if (qk) {
+        MapRoot& r = p.m.roots[0];
+        const int64_t lo0 = r.begin, hi0 = r.end < 0 ? n : r.end;
+        const int64_t base = sh.u0 * m0.n, top = sh.u1 * m0.n;
+        const int64_t lo = lo0 > base ? lo0 : base, hi = hi0 < top ? hi0 : top;
+        r.begin = hi > lo ? lo - base : 0;
+        r.end = hi > lo ? hi - base : 0;
+        scPartial = r.begin != 0 || r.end != units * m0.n;
+    }
+    for (size_t i = 0; i < nb; ++i) {
+        const int bid = m0.bindable[i];
+        int64_t rowLen = 1;
+        if (bid == m0.callA) rowLen = m0.k;
+        else if (bid == m0.callOut) rowLen = (m0.kind == MLKB_KIND_MATMUL || qk) ? m0.n
+                                             : m0.kind == MLKB_KIND_SOFTMAX ? m0.k : 1;
+        else if (qk && (bid == m0.qkS || bid == m0.qkSc)) rowLen = m0.n;
+        BufPlan& b = p.b[i];
+        if (bid == m0.callB) {
+            b.off = 0;
+            b.cnt = m0.k * m0.n;
+        } else {
+            b.off = sh.u0 * rowLen;
+            b.cnt = units * rowLen;
+        }
+        b.in = m0.buffers[bid].input;
+        b.out = m0.buffers[bid].output;
+        b.rmw = (m0.kind == MLKB_KIND_MATMUL && bid == m0.callOut) || (qk && bid == m0.qkS) ||
+                (qk && scPartial && bid == m0.qkSc);
+    }
+    return p;
+}
+
+int runAssembled(const Module& m, void* const* bufs, const int32_t* dt, int32_t n_bufs, int64_t n,
+                 const double* scalars, int64_t n_scalars, int32_t n_gpus) {
+    if (n_bufs != static_cast<int32_t>(m.bindable.size())) {
+        return setError(MLKB_ERR_INVALID, "run_sharded: buffer count differs from the module table");
+    }
+    for (int32_t i = 0; i < n_bufs; ++i) {
+        if (bufs[i] == nullptr) return setError(MLKB_ERR_INVALID, "run_sharded: null buffer");
+        if (elemBytes(dt[i]) == 0) return setError(MLKB_ERR_INVALID, "run_sharded: unknown dtype");
+    }
+    if (int st = validateRun(m, dt, n)) return st;
+    std::lock_guard<std::mutex> lock(g_ncclMu);
+    const NcclApi& api = ncclApi();
+    if (!api.ok) return setError(MLKB_ERR_NCCL, api.err.c_str());
+    const int avail = deviceCount();
+    if (avail <= 0) return setError(MLKB_ERR_NO_DEVICE, "no CUDA device");
+    int g = n_gpus <= 0 ? avail : (n_gpus < avail ? n_gpus : avail);
+    const int64_t units = unitsOf(m, n);
+    if (units < 0) return setError(MLKB_ERR_UNSUPPORTED, "run_sharded: module kind not runnable here");
+    // Every output must be device memory on device 0.
+    for (int32_t i = 0; i < n_bufs; ++i) {
+        if (!m.buffers[m.bindable[i]].output) continue;
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, bufs[i]) != cudaSuccess ||
+            at.type != cudaMemoryTypeDevice || at.device != 0) {
+            cudaGetLastError();
+            return setError(MLKB_ERR_INVALID,
+                            "run_sharded: assembled outputs must be device memory on device 0");
+        }
+    }
+    std::vector<ncclComm_t>* comms = nullptr;
+    if (int st = ncclClique(api, g, &comms)) return st;
+    if (units == 0) return okStatus();
+    if (g > units) g = static_cast<int>(units);
+    std::vector<ShardPlan> plans;
+    for (int d = 0; d < g; ++d) {
+        const int64_t u0 = shardEdge(m, units, d, g), u1 = shardEdge(m, units, d + 1, g);
+        if (u1 > u0) plans.push_back(planShard(m, Shard{d, u0, u1}, n));
+    }
+    // Device contexts 0..g-1 in increasing order (the host-buffer path takes
+    // one at a time); device 0 always takes part, a shard of its own or not.
+    std::vector<std::unique_lock<std::mutex>> held;
+    for (int d = 0; d < g; ++d) {
+        held.emplace_back(g_dev[d].mu);
+        if (cudaSetDevice(d) != cudaSuccess) return setError(MLKB_ERR_NO_DEVICE, "cudaSetDevice");
+        if (int st = ensureCtx(d)) return st;
+    }
+    const cudaStream_t s0 = g_dev[0].streams[0];
+    cudaError_t e = cudaSuccess;
+    auto bytes = [&](size_t i, const BufPlan& b) { return static_cast<size_t>(b.cnt) * elemBytes(dt[i]); };
+    // 1. slots and host inputs
+    for (ShardPlan& p : plans) {
+        cudaSetDevice(p.dev);
+        p.st = g_dev[p.dev].streams[0];
+        for (size_t i = 0; i < p.b.size(); ++i) {
+            BufPlan& b = p.b[i];
+            if (int st = slotPtr(p.dev, i, bytes(i, b), &b.slot)) return st;
+            if (b.in && b.cnt > 0) {
+                e = cudaMemcpyAsync(b.slot, offsetPtr(bufs[i], b.off, dt[i]), bytes(i, b),
+                                    cudaMemcpyHostToDevice, p.st);
+                if (e != cudaSuccess) return setCudaError(MLKB_ERR_CUDA_MEM, e, "H2D");
+            }
+        }
+    }
+    // 2 and 4: device 0 <-> every shard, one NCCL group per direction
+    auto exchange = [&](bool scatter) -> int {
+        ncclResult_t r = api.groupStart();
+        if (r != ncclSuccess) return ncclFail(api, r, "ncclGroupStart");
+        int rc = MLKB_OK;
+        for (ShardPlan& p : plans) {
+            for (size_t i = 0; i < p.b.size() && rc == MLKB_OK; ++i) {
+                const BufPlan& b = p.b[i];
+                if (!(scatter ? b.rmw : b.out) || b.cnt == 0) continue;
+                char* home = offsetPtr(bufs[i], b.off, dt[i]);
+                if (p.dev == 0) {
+                    cudaSetDevice(0);
+                    e = cudaMemcpyAsync(scatter ? b.slot : home, scatter ? home : b.slot,
+                                        bytes(i, b), cudaMemcpyDeviceToDevice, p.st);
+                    if (e != cudaSuccess) rc = setCudaError(MLKB_ERR_CUDA_MEM, e, "D2D");
+                    continue;
+                }
+                const ncclComm_t c0 = (*comms)[0], cd = (*comms)[static_cast<size_t>(p.dev)];
+                r = scatter ? api.send(home, bytes(i, b), ncclUint8, p.dev, c0, s0)
+                            : api.recv(home, bytes(i, b), ncclUint8, p.dev, c0, s0);
+                if (r == ncclSuccess) {
+                    r = scatter ? api.recv(b.slot, bytes(i, b), ncclUint8, 0, cd, p.st)
+                                : api.send(b.slot, bytes(i, b), ncclUint8, 0, cd, p.st);
+                }
+                if (r != ncclSuccess) rc = ncclFail(api, r, scatter ? "scatter" : "gather");
+            }
+        }
+        r = api.groupEnd();
+        if (rc == MLKB_OK && r != ncclSuccess) rc = ncclFail(api, r, "ncclGroupEnd");
+        return rc;
+    };
+    if (int st = exchange(true)) return st;
+    // 3. every shard computes
+    for (ShardPlan& p : plans) {
+        cudaSetDevice(p.dev);
+        std::vector<void*> slots(p.b.size());
+        for (size_t i = 0; i < p.b.size(); ++i) slots[i] = p.b[i].slot;
+        if (int rs = runDev(p.m, slots.data(), dt, p.m.kind == MLKB_KIND_MAP ? units : n, scalars,
+                            n_scalars, p.st)) {
+            return rs;
+        }
+    }
+    if (int st = exchange(false)) return st;
+    for (int d = 0; d < g; ++d) {
+        cudaSetDevice(d);
+        e = cudaStreamSynchronize(g_dev[d].streams[0]);
+        if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "assembled run sync");
+    }
+    return okStatus();
+}
+
 // ---- reference artifact ABI state --------------------------------------------
 std::mutex g_bindMu;
 std::shared_ptr<mlkb_module> g_bound;
@@ -880,6 +1157,23 @@ extern "C" int mlkb_module_run_host(const mlkb_module* module, void* const* bufs
     }
     if (n < 0) return setError(MLKB_ERR_INVALID, "run_host: negative element count");
     return runHost(module->m, bufs, dtypes, n_bufs, n, scalars, n_scalars, n_gpus);
+}
+
+extern "C" int mlkb_module_run_sharded(const mlkb_module* module, void* const* bufs,
+                                       const int32_t* dtypes, int32_t n_bufs, int64_t n,
+                                       const double* scalars, int64_t n_scalars, int32_t n_gpus,
+                                       uint32_t flags) {
+    if (module == nullptr || bufs == nullptr || dtypes == nullptr) {
+        return setError(MLKB_ERR_INVALID, "run_sharded: null argument");
+    }
+    if (n < 0) return setError(MLKB_ERR_INVALID, "run_sharded: negative element count");
+    if ((flags & ~static_cast<uint32_t>(MLKB_ASSEMBLE_DEVICE0)) != 0) {
+        return setError(MLKB_ERR_INVALID, "run_sharded: unknown flag");
+    }
+    if ((flags & MLKB_ASSEMBLE_DEVICE0) == 0) {
+        return runHost(module->m, bufs, dtypes, n_bufs, n, scalars, n_scalars, n_gpus);
+    }
+    return runAssembled(module->m, bufs, dtypes, n_bufs, n, scalars, n_scalars, n_gpus);
 }
 
 extern "C" int mlk_bind_module(const char* json) {

@@ -195,6 +195,25 @@ def merge_roots(modules, names=None) -> dict:
             "buffers": bufs, "nodes": nodes, "schedule": dict(first.get("schedule", {}))}
 
 
+def with_static_length(module: dict, n: int) -> dict:
+    """A copy of a module compiled for a tensor of static length n0 (loop
+    bounds and buffer sizes fixed at n0, as the reference's pipeline emits
+    them) with every such n0 replaced by n: the document the same pipeline
+    writes for a tensor of length n (its output differs only in those
+    numbers)."""
+    m = json.loads(json.dumps(module))
+    n0 = m["buffers"][0]["elements"]
+    for b in m["buffers"]:
+        if b.get("elements") == n0:
+            b["elements"] = int(n)
+        if b.get("dims") == [n0]:
+            b["dims"] = [int(n)]
+    for node in m["nodes"]:
+        if node["op"] == "loop" and node.get("end") == n0:
+            node["end"] = int(n)
+    return m
+
+
 def chains_of(module: dict):
     """The expression chain of each Compute node, as mlkb_expr arrays (for
     running a module's chains through the oracle)."""

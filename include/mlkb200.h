@@ -271,6 +271,34 @@ int mlkb_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols,
 int mlkb_softmax_f64(const double* x, double* y, int64_t rows, int64_t cols,
                      void* stream);
 
+/*
+ * The row softmax of mlkb_softmax_f32 for callers that cannot allocate device
+ * memory: a process whose device memory is all handed out by its own pool
+ * allocator, a plugin host whose execute callback must not call cudaMalloc,
+ * or code that may not pay the device-wide synchronisation cudaMalloc implies.
+ * mlkb_softmax_f32 obtains its kernel's status word with cudaMalloc on its
+ * first call on each device; this entry keeps that scratch in a fixed 256-byte
+ * array of the library instead (each GPU that loads the library holds one
+ * until the process exits) and calls no cudaMalloc, cudaFree or other
+ * allocating routine. No counterpart in the reference (its emitted artifacts
+ * allocate and free on every call).
+ *   rows, cols   at most 8192 columns, a multiple of 4, x and y 16-byte
+ *                aligned; anything else returns MLKB_ERR_INVALID (use
+ *                mlkb_softmax_f32 for it). The kernel needs 4 bytes of the
+ *                scratch whatever the shape.
+ *   wait         0: returns once the kernel is queued on `stream`, and a
+ *                bounded device wait that gives up is not reported; nonzero:
+ *                synchronises `stream` and returns the kernel's device status
+ *                (MLKB_ERR_TIMEOUT if one of its waits gave up).
+ * The first call on each device looks up the scratch's device address with
+ * that device current (no allocation); make that first call before any
+ * stream capture. All calls on a device share the one array: each call clears
+ * the status word before its kernel, so calls that overlap on the GPU (other
+ * streams or threads) race on it.
+ */
+int mlkb_softmax_f32_noalloc(const float* x, float* y, int64_t rows, int64_t cols,
+                             int32_t wait, void* stream);
+
 /* Row sums Y[m] = sum_k X[m,k] (reference execReduceSumCall,
  * kernel_buffers.cpp:237-277). */
 int mlkb_reducesum_f32(const float* x, float* y, int64_t rows, int64_t cols,

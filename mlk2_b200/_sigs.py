@@ -29,6 +29,7 @@ SIGNATURES = {
     "mlkb_map_chain": (i32, [vp, i32, i32, vp, vp, vp, i32, i64, C.POINTER(f64), i64, vp]),
     "mlkb_softmax_f32": (i32, [vp, vp, i64, i64, vp]),
     "mlkb_softmax_f64": (i32, [vp, vp, i64, i64, vp]),
+    "mlkb_softmax_f32_noalloc": (i32, [vp, vp, i64, i64, i32, vp]),
     "mlkb_reducesum_f32": (i32, [vp, vp, i64, i64, vp]),
     "mlkb_reducesum_f64": (i32, [vp, vp, i64, i64, vp]),
     "mlkb_gemm_f16_f32": (i32, [vp, vp, vp, i64, i64, i64, i32, vp]),

@@ -14,6 +14,7 @@
 // Rows that do not fit the register tile (or are not float4-aligned) take a
 // three-pass streaming kernel with the same arithmetic.
 #include <atomic>
+#include <mutex>
 
 #include "common.cuh"
 #include "tc_common.cuh"
@@ -392,4 +393,102 @@ extern "C" int mlkb_reducesum_f64(const double* x, double* y, int64_t rows, int6
     reducesum_rows<double><<<static_cast<int>(blocks < 65535 ? blocks : 65535), 128, 0,
                              asStream(stream)>>>(x, y, rows, cols);
     return checkLaunch("reducesum f64 launch");
+}
+
+// ---- allocation-free entry ---------------------------------------------------------
+// mlkb_softmax_f32 and the other entries whose kernels have bounded waits keep
+// their status word in device memory the library obtains with cudaMalloc on
+// the first call on each device. This entry runs the same TMA row kernel with
+// that scratch in a fixed array of this file instead, so it never allocates.
+namespace mlkb {
+namespace {
+
+// The scratch of mlkb_softmax_f32_noalloc: 256 bytes, of which the kernel
+// uses the first word (the status its bounded waits report through, whatever
+// the shape). Every device that loads the library holds one copy until the
+// process exits. In host code this name is only a stand-in for the symbol:
+// kernels get the device address from cudaGetSymbolAddress below.
+constexpr size_t kNoAllocScratchBytes = 256;
+constexpr size_t kNoAllocStatusBytes = sizeof(int);
+static_assert(kNoAllocStatusBytes <= kNoAllocScratchBytes, "status word fits the scratch");
+static __device__ __align__(256) int g_softmax_noalloc_scratch[kNoAllocScratchBytes / sizeof(int)];
+
+// Device address of the scratch on the current device, looked up once per
+// device (with that device current) and kept.
+int noAllocScratch(int** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return setCudaError(MLKB_ERR_NO_DEVICE, e, "softmax_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= 64) return setError(MLKB_ERR_INVALID, "softmax_noalloc: device index past 63");
+    static std::mutex mu;
+    static int* addr[64] = {nullptr};
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_softmax_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            return setCudaError(MLKB_ERR_LAUNCH, e, "softmax_noalloc: cudaGetSymbolAddress");
+        }
+        addr[dev] = static_cast<int*>(p);
+    }
+    *out = addr[dev];
+    return okStatus();
+}
+
+template <int NV, bool kFull>
+int launchRowsNoAlloc(const float* x, float* y, int64_t rows, int64_t cols, int* status,
+                      cudaStream_t s) {
+    const uint32_t buf = ((static_cast<uint32_t>(cols) * 4u + 127u) & ~127u);
+    const size_t smem = 2 * static_cast<size_t>(buf);
+    static std::atomic<bool> attr[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(softmax_rows_tma<NV, kFull>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   64 * 1024);
+        if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "softmax_noalloc smem attribute");
+        attr[dev] = true;
+    }
+    const int per_sm = 4 * (NV <= 2 ? 8 : NV <= 4 ? 6 : 3);
+    softmax_rows_tma<NV, kFull><<<rowGrid(rows, per_sm), kRowThreads, smem, s>>>(x, y, rows,
+                                                                                 cols, status);
+    return checkLaunch("softmax_noalloc launch");
+}
+
+template <int NV>
+int launchRowsNoAlloc(const float* x, float* y, int64_t rows, int64_t cols, int* status,
+                      cudaStream_t s) {
+    return cols == NV * 4 * kRowThreads ? launchRowsNoAlloc<NV, true>(x, y, rows, cols, status, s)
+                                        : launchRowsNoAlloc<NV, false>(x, y, rows, cols, status, s);
+}
+
+}  // namespace
+}  // namespace mlkb
+
+extern "C" int mlkb_softmax_f32_noalloc(const float* x, float* y, int64_t rows, int64_t cols,
+                                        int32_t wait, void* stream) {
+    using namespace mlkb;
+    if (int st = checkRows(x, y, rows, cols)) return st;
+    if (cols > 8192 || cols % 4 != 0 || !aligned16(x) || !aligned16(y)) {
+        return setError(MLKB_ERR_INVALID,
+                        "softmax_noalloc: rows of at most 8192 columns, a multiple of 4, with "
+                        "16-byte aligned buffers (other shapes: mlkb_softmax_f32)");
+    }
+    int* status = nullptr;
+    if (int st = noAllocScratch(&status)) return st;
+    cudaStream_t s = asStream(stream);
+    // The status word must start at zero on every call.
+    cudaError_t e = cudaMemsetAsync(status, 0, kNoAllocStatusBytes, s);
+    if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "softmax_noalloc: clear status");
+    int rc = cols <= 1024   ? launchRowsNoAlloc<1>(x, y, rows, cols, status, s)
+             : cols <= 2048 ? launchRowsNoAlloc<2>(x, y, rows, cols, status, s)
+             : cols <= 4096 ? launchRowsNoAlloc<4>(x, y, rows, cols, status, s)
+                            : launchRowsNoAlloc<8>(x, y, rows, cols, status, s);
+    if (rc != MLKB_OK || wait == 0) return rc;
+    int word = 0;
+    e = cudaMemcpyAsync(&word, status, sizeof(word), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "softmax_noalloc: status read");
+    return word == 0 ? okStatus() : setError(word, "softmax_noalloc: a bounded device wait gave up");
 }

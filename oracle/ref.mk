@@ -10,7 +10,9 @@
 # objects are written under oracle/_ref/obj/.
 #
 #   make -f oracle/ref.mk REF=/path/to/reference -j8
-REF      ?= /root/reference
+ifeq ($(strip $(REF)),)
+$(error REF=<reference source tree> is required)
+endif
 OUT      ?= oracle/_ref
 CXX      ?= g++
 CXXFLAGS ?= -std=c++23 -O2 -fPIC -fno-exceptions -fno-rtti -w -pthread

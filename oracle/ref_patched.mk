@@ -14,6 +14,8 @@
 #                       (Tier1 modules), and a declared ULP-bounded identity
 #                       policy for Cuda candidates
 #   03-multi-output-lowering  each output's Store / Call targets its own buffer
+#   04-poly-bench-b200  `mlk-poly bench --b200-lib=L`: a b200 row per case and
+#                       a suite at BASELINE shapes (built here as mlk-poly)
 ifeq ($(strip $(REF)),)
 $(error REF=<reference source tree> is required)
 endif
@@ -22,7 +24,7 @@ SRC      := $(OUT)/src
 CXX      ?= g++
 CXXFLAGS ?= -std=c++23 -O2 -fPIC -fno-exceptions -fno-rtti -w -pthread
 PATCHES  := $(sort $(wildcard oracle/ref_patches/*.patch))
-DIRS     := compiler runtime backends polyhedral autotuner superopt fastkernel
+DIRS     := compiler runtime backends polyhedral autotuner superopt fastkernel tools
 
 all: $(SRC)/.applied
 	@$(MAKE) --no-print-directory -f oracle/ref_patched.mk REF=$(REF) build
@@ -54,7 +56,11 @@ $(OUT)/ref_integration_check: oracle/ref_integration_check.cpp oracle/ref_module
 	$(CXX) $(CXXFLAGS) $(INCS) oracle/ref_integration_check.cpp $(OUT)/libmlkref_patched.a \
 	  -ldl -o $@
 
-build: $(OUT)/ref_integration_check
+POLY := $(wildcard $(SRC)/tools/mlk-poly/*.cpp)
+$(OUT)/mlk-poly: $(POLY) $(OUT)/libmlkref_patched.a
+	$(CXX) $(CXXFLAGS) $(INCS) $(POLY) $(OUT)/libmlkref_patched.a -ldl -o $@
+
+build: $(OUT)/ref_integration_check $(OUT)/mlk-poly
 endif
 
 .PHONY: all build

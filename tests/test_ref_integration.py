@@ -84,3 +84,47 @@ def test_fastkernel_certifies_the_cuda_variant(cuda):
     assert sin["policy"] == "ulp-bounded-f64-cuda-v1" and sin["max_ulp"] <= 16
     for g in ("gemm_64x48x56", "map_sin_4096"):
         assert by[(g, "walker")]["identity"]
+
+
+POLY = os.path.join(os.path.dirname(CHECK), "mlk-poly")
+needs_poly = pytest.mark.skipif(not os.path.exists(POLY),
+                                reason="patched mlk-poly not built (reference sources absent)")
+
+
+def poly_bench(tmp_path, suites):
+    """The reference's own benchmark front end (patched: 04-poly-bench-b200)
+    with libmlkb200 as its b200 row. nvcc is kept off PATH, so the reference's
+    own emitted CUDA artifact (never run on a device by the reference) is
+    reported as an honest skip instead of being run."""
+    env = dict(os.environ, PATH="/usr/bin:/bin", MLK_B200_LIBRARY=mb.LIB_PATH,
+               MLK_BACKEND_WORKDIR=str(tmp_path))
+    out_json = tmp_path / "rows.json"
+    subprocess.run([POLY, "bench", "--reps=3", "--warmup=1", f"--suites={suites}",
+                    f"--json-out={out_json}"], env=env, capture_output=True, text=True,
+                   timeout=900)
+    return json.loads(out_json.read_text())["rows"]
+
+
+@needs_poly
+@pytest.mark.skipif(mb.lib().mlkb_device_count() > 0, reason="host without a GPU only")
+def test_poly_bench_b200_rows_without_a_device(tmp_path):
+    rows = poly_bench(tmp_path, "softmax")
+    b200 = [r for r in rows if r["path"] == "b200"]
+    assert len(b200) == 2 and all("code 4" in r["note"] and not r["timed"] for r in b200)
+
+
+@needs_poly
+@pytest.mark.gpu
+def test_poly_bench_b200_rows(cuda, tmp_path):
+    rows = poly_bench(tmp_path, "gemm,softmax,reducesum,baseline")
+    b200 = {(r["suite"], r["shape"]): r for r in rows if r["path"] == "b200"}
+    tier1 = {(r["suite"], r["shape"]) for r in rows if r["path"] == "tier1" and r["timed"]}
+    assert set(b200) == tier1 and ("gemm", "1024x1024x1024") in b200
+    for key, r in b200.items():
+        assert r["timed"], (key, r["note"])
+        if key[0] in ("gemm", "reducesum"):
+            assert r["bitexact"] and r["note"] == "bit-exact", (key, r)
+        else:  # f64 softmax: CUDA exp vs glibc exp
+            assert r["note"] == "bit-exact" or float(r["note"].split("=")[1].split()[0]) <= 64
+    cuda_rows = [r for r in rows if r["path"] == "cuda"]
+    assert all(r["note"] == "cuda-toolchain-unavailable" for r in cuda_rows)

@@ -223,9 +223,9 @@ softmax_rows_tma(const float* __restrict__ x, float* __restrict__ y, int64_t row
     }
 }
 
-// Exponential used by the streaming kernel: the f32 path uses the same
-// f64 routine as the register kernel; the f64 path (reference-facing f64 ABI)
-// calls CUDA's double exp and divides exactly like the reference.
+// Exponential and final scaling of the streaming kernel (f32 rows that the
+// register kernel does not take): the same f64 routine as the register
+// kernel. The f64 rows have their own kernel below.
 template <typename T>
 struct SoftmaxMath;
 
@@ -235,12 +235,6 @@ struct SoftmaxMath<float> {
     __device__ static float out(double e, double s) {
         return s != 0.0 ? static_cast<float>(e * (1.0 / s)) : 0.0f;
     }
-};
-
-template <>
-struct SoftmaxMath<double> {
-    __device__ static double ex(double d) { return ::exp(d); }
-    __device__ static double out(double e, double s) { return s != 0.0 ? e / s : 0.0; }
 };
 
 // Three-pass streaming row softmax, any cols and alignment: max, sum, write.
@@ -283,6 +277,59 @@ softmax_rows_stream(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
         }
     }
     (void)smax;
+}
+
+// f64 row softmax in the reference's own order (execSoftmaxCall,
+// kernel_buffers.cpp:317-339): the row max (exact in any order; a NaN never
+// wins the select, and the sign of a zero maximum does not change x - r),
+// e = exp(x - r) written into the output row, the sum of the row's e in
+// ASCENDING k by one thread, then y = e / s (0 when s == 0); in place (x ==
+// y) too, as each element is read before it is written. Only the
+// exponential (CUDA's against the reference host's libm) can differ, so the
+// result stays within a few f64 ULP whatever the row length; a tree sum
+// drifts by up to ~cols * 2^-53. This is the reference-ABI path, not a
+// throughput kernel: the ascending sum is one dependent chain per row.
+constexpr int kRefRowThreads = 128;
+
+__global__ void __launch_bounds__(kRefRowThreads)
+softmax_rows_f64_ref(const double* __restrict__ x, double* __restrict__ y, int64_t rows,
+                     int64_t cols) {
+    __shared__ double smax[kRefRowThreads / 32];
+    __shared__ double ssum;
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const double* xr = x + row * cols;
+        double* yr = y + row * cols;
+        double m = -INFINITY;
+        for (int64_t c = threadIdx.x; c < cols; c += kRefRowThreads) {
+            const double v = xr[c];
+            m = (v > m) ? v : m;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const double w = __shfl_xor_sync(0xffffffffu, m, o);
+            m = (w > m) ? w : m;
+        }
+        if ((threadIdx.x & 31) == 0) smax[threadIdx.x >> 5] = m;
+        __syncthreads();
+        m = smax[0];
+#pragma unroll
+        for (int i = 1; i < kRefRowThreads / 32; ++i) m = (smax[i] > m) ? smax[i] : m;
+        for (int64_t c = threadIdx.x; c < cols; c += kRefRowThreads) {
+            yr[c] = ::exp(__dsub_rn(xr[c], m));
+        }
+        __syncthreads();  // the row's e are in y, visible to the whole block
+        if (threadIdx.x == 0) {
+            double acc = 0.0;
+            for (int64_t c = 0; c < cols; ++c) acc = __dadd_rn(acc, yr[c]);
+            ssum = acc;
+        }
+        __syncthreads();
+        const double sum = ssum;
+        for (int64_t c = threadIdx.x; c < cols; c += kRefRowThreads) {
+            yr[c] = sum != 0.0 ? __ddiv_rn(yr[c], sum) : 0.0;
+        }
+        __syncthreads();  // smax / ssum are reused by the next row
+    }
 }
 
 // Row sums in ascending k, one thread per row, f64 accumulation: the
@@ -370,7 +417,7 @@ extern "C" int mlkb_softmax_f64(const double* x, double* y, int64_t rows, int64_
                                 void* stream) {
     using namespace mlkb;
     if (int st = checkRows(x, y, rows, cols)) return st;
-    softmax_rows_stream<double><<<rowGrid(rows, 8), kRowThreads, 0, asStream(stream)>>>(
+    softmax_rows_f64_ref<<<rowGrid(rows, 16), kRefRowThreads, 0, asStream(stream)>>>(
         x, y, rows, cols);
     return checkLaunch("softmax f64 launch");
 }

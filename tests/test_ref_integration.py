@@ -124,7 +124,7 @@ def test_poly_bench_b200_rows(cuda, tmp_path):
         assert r["timed"], (key, r["note"])
         if key[0] in ("gemm", "reducesum"):
             assert r["bitexact"] and r["note"] == "bit-exact", (key, r)
-        else:  # f64 softmax: CUDA exp vs glibc exp
-            assert r["note"] == "bit-exact" or float(r["note"].split("=")[1].split()[0]) <= 64
+        else:  # f64 softmax: only CUDA's exp differs from the host libm's
+            assert r["note"] == "bit-exact" or float(r["note"].split("=")[1].split()[0]) <= 8
     cuda_rows = [r for r in rows if r["path"] == "cuda"]
     assert all(r["note"] == "cuda-toolchain-unavailable" for r in cuda_rows)

@@ -62,7 +62,7 @@ def test_softmax_f64_and_reducesum(cuda, golden):
     x = dev(cuda, g["rand_x"].astype(np.float64))
     y = empty(cuda, x.shape, cuda.float64)
     api.softmax(x, y)
-    assert oracle.ulp_f64(host(y), g["rand_y"]).max() <= 64
+    assert oracle.ulp_f64(host(y), g["rand_y"]).max() <= 8   # only exp differs (same order)
     r = golden("reducesum")
     for dt, npdt in ((cuda.float32, np.float32), (cuda.float64, np.float64)):
         xr = dev(cuda, r["x"].astype(npdt))
@@ -86,4 +86,4 @@ def test_softmax_module_paths(cuda, golden):
     y64 = np.zeros(xh.shape, np.float64)
     assert api.legacy_call(kir.call_module("softmax", *xh.shape, dtypes=("f64", "f64")),
                            [xh.astype(np.float64), y64], xh.size) == mb.OK
-    assert oracle.ulp_f64(y64, g["rand_y"]).max() <= 64
+    assert oracle.ulp_f64(y64, g["rand_y"]).max() <= 8

@@ -340,7 +340,7 @@ def main():
                     help="headline warm-up continues at least this long (clock samples); "
                          "also the run-in of each config's sustained figure (0: none)")
     ap.add_argument("--case", default=None,
-                    choices=["map1", "map2", "softmax", "gemm", "gemm_f32", "qk"],
+                    choices=["map1", "map2", "softmax", "gemm", "gemm_f32", "qk", "qk_kt"],
                     help="run one kernel W+K times (profiling target), no JSON line")
     ap.add_argument("--detail", default=None,
                     help="also write the full (verbose) record as JSON to this path")
@@ -663,7 +663,11 @@ def run_case(args):
         q.normal_()
         k.normal_()
         yq = torch.empty((bq, 2048, 2048), device="cuda")
-        fn = lambda: api.qk_softmax(q, k, yq, 128 ** -0.5)  # noqa: E731
+        if c == "qk":
+            fn = lambda: api.qk_softmax(q, k, yq, 128 ** -0.5)  # noqa: E731
+        else:  # K given as the reference's MatMul B operand, Kt [batch, d, s]
+            kt = k.transpose(1, 2).contiguous()
+            fn = lambda: api.qk_softmax_kt(q, kt, yq, 128 ** -0.5)  # noqa: E731
     sec = time_device(torch, fn, args.warmup, args.steps, None, 1)
     print(json.dumps({"case": c, "size": sz, "ms_per_launch": sec * 1e3}), flush=True)
 

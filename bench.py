@@ -436,7 +436,7 @@ def main():
     plan = module.plan([mb.F32] * 3)
     # device-timed run of the same module through mlkb_module_run_dev
     ym, dym = torch.empty_like(x), torch.empty_like(x)
-    msec = time_device(torch, lambda: module.run_dev([x, ym, dym], n=n), args.warmup,
+    msec = time_device(torch, lambda: module.run_dev([x, ym, dym], n=n, device=local), args.warmup,
                        args.steps, dist, world)
     module_dev = {"plan": plan, "ms": msec * 1e3,
                   "f": alg_bytes / msec / 1e9 / peaks["hbm_gbs"]}

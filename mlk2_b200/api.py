@@ -164,8 +164,16 @@ class Module:
         sc = (C.c_double * max(1, len(scalars)))(*scalars)
         return ptrs, dts, n, sc
 
-    def run_dev(self, bufs, n: int = 0, scalars: Sequence[float] = (), device: int = 0,
+    def run_dev(self, bufs, n: int = 0, scalars: Sequence[float] = (), device=None,
                 stream=None):
+        """Runs over device tensors on `device` (default: the tensors' own
+        device) and `stream` (default: torch's current stream of it)."""
+        if device is None:
+            device = next((b.device.index for b in bufs if hasattr(b, "device")), 0)
+        if stream is None:
+            import torch
+
+            stream = torch.cuda.current_stream(device).cuda_stream
         ptrs, dts, nb, sc = self._args(bufs, scalars)
         check(lib().mlkb_module_run_dev(self._h, ptrs, dts, nb, n, sc, len(scalars), device,
                                         _stream(stream)))

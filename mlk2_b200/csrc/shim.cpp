@@ -110,6 +110,42 @@ int deviceCount() {
     return n;
 }
 
+// Restores the calling thread's current device when it goes out of scope:
+// an entry point never leaves the caller on another device.
+struct DeviceGuard {
+    int saved = -1;
+    DeviceGuard() {
+        if (cudaGetDevice(&saved) != cudaSuccess) {
+            saved = -1;
+            cudaGetLastError();
+        }
+    }
+    ~DeviceGuard() {
+        if (saved >= 0) cudaSetDevice(saved);
+    }
+};
+
+// Every buffer must be memory `device` can address: device memory of that
+// device, or managed memory. Anything else (another GPU's memory, host
+// memory) would fault in a kernel on `device` instead of failing here.
+int checkBuffersOn(int device, void* const* bufs, int32_t n_bufs) {
+    for (int32_t i = 0; i < n_bufs; ++i) {
+        if (bufs[i] == nullptr) continue;
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, bufs[i]) != cudaSuccess) {
+            cudaGetLastError();
+            return setError(MLKB_ERR_INVALID, "run_dev: a buffer is not CUDA-visible memory");
+        }
+        const bool ok = at.type == cudaMemoryTypeManaged ||
+                        (at.type == cudaMemoryTypeDevice && at.device == device);
+        if (!ok) {
+            return setError(MLKB_ERR_INVALID,
+                            "run_dev: every buffer must be device memory of the given device");
+        }
+    }
+    return okStatus();
+}
+
 int ensureCtx(int dev) {
     DeviceCtx& c = g_dev[dev];
     if (c.init) return okStatus();
@@ -958,6 +994,7 @@ int runAssembled(const Module& m, void* const* bufs, const int32_t* dt, int32_t 
         if (elemBytes(dt[i]) == 0) return setError(MLKB_ERR_INVALID, "run_sharded: unknown dtype");
     }
     if (int st = validateRun(m, dt, n)) return st;
+    DeviceGuard guard;  // the device loop below switches devices
     std::lock_guard<std::mutex> lock(g_ncclMu);
     const NcclApi& api = ncclApi();
     if (!api.ok) return setError(MLKB_ERR_NCCL, api.err.c_str());
@@ -1144,6 +1181,15 @@ extern "C" int mlkb_module_run_dev(const mlkb_module* module, void* const* bufs,
     const int avail = deviceCount();
     if (avail <= 0) return setError(MLKB_ERR_NO_DEVICE, "no CUDA device");
     if (device < 0 || device >= avail) return setError(MLKB_ERR_INVALID, "run_dev: bad device");
+    if (int st = checkBuffersOn(device, bufs, n_bufs)) return st;
+    if (stream != nullptr) {
+        int sdev = -1;
+        if (cudaStreamGetDevice(asStream(stream), &sdev) != cudaSuccess || sdev != device) {
+            cudaGetLastError();
+            return setError(MLKB_ERR_INVALID, "run_dev: the stream belongs to another device");
+        }
+    }
+    DeviceGuard guard;
     const cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) return setCudaError(MLKB_ERR_NO_DEVICE, e, "cudaSetDevice");
     return runDev(module->m, bufs, dtypes, n, scalars, n_scalars, stream);

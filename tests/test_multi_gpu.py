@@ -44,3 +44,34 @@ def test_sharded_host_runs_match_single_gpu(cuda, n_gpus):
     c = c0.copy()
     mm.run_host([a, b, c], n_gpus=n_gpus)
     assert np.array_equal(c, oracle.port().matmul(a, b, c0))
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
+def test_device_checks_and_current_device_kept(cuda):
+    """A kernel never runs on one GPU against another GPU's buffers: run_dev
+    refuses buffers (or a stream) of another device, and no entry point leaves
+    the caller on a different current device."""
+    import ctypes as C
+
+    m = api.Module(kir.map_module([kir.SIN_CHAIN]))
+    x1 = cuda.zeros(1024, device="cuda:1")
+    y1 = cuda.zeros(1024, device="cuda:1")
+    ptrs = (C.c_void_p * 2)(x1.data_ptr(), y1.data_ptr())
+    dts = (C.c_int32 * 2)(mb.F32, mb.F32)
+    sc = (C.c_double * 1)(0.0)
+    cuda.cuda.set_device(0)
+    st = mb.lib().mlkb_module_run_dev(m._h, ptrs, dts, 2, 1024, sc, 0, 0, None)
+    assert st == mb.ERR_INVALID
+    s1 = cuda.cuda.Stream(device=1)
+    ptrs0 = (C.c_void_p * 2)(cuda.zeros(1024, device="cuda:0").data_ptr(),
+                             cuda.zeros(1024, device="cuda:0").data_ptr())
+    st = mb.lib().mlkb_module_run_dev(m._h, ptrs0, dts, 2, 1024, sc, 0, 0, s1.cuda_stream)
+    assert st == mb.ERR_INVALID
+    # the right device and stream run, and the caller's device is kept
+    m.run_dev([x1, y1], n=1024, device=1)
+    assert cuda.cuda.current_device() == 0
+    xs = np.linspace(-8, 8, 4096).astype(np.float32)
+    out = [cuda.zeros(4096, device="cuda:0"), cuda.zeros(4096, device="cuda:0")]
+    two = api.Module(kir.map_module([kir.SIN_CHAIN, kir.DSIN_CHAIN]))
+    assert two.run_sharded([xs] + out, n=4096, n_gpus=2) == 0
+    assert cuda.cuda.current_device() == 0

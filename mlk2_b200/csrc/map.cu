@@ -10,13 +10,18 @@
 //     forms it (x*x and 3x are exact in f64 for f32 x, so one FMA reproduces
 //     the Add's single rounding), sin/cos of u in f64, one final rounding to
 //     f32. HBM-bound: 8 B (map) or 12 B (map + derivative) per element.
-//   * a generic chain interpreter for any chain of scalar-realisable ops,
+//   * a generic chain interpreter for any chain of scalar-realisable ops
+//     (register-slot form for chains with at most 8 temps alive at once and
+//     16-byte aligned buffers, a local-array form otherwise),
 //     f32 or f64 buffers, with the reference's guarded semantics
 //     (Div by 0 -> 0, Log of <= 0 -> 0, Sqrt of < 0 -> 0, Rsqrt of <= 0 -> 0,
 //     Pow(2,2) -> a*a). Add/Sub/Mul/Div use round-to-nearest intrinsics so
 //     no FMA contraction changes a rounding: arithmetic-only chains are
 //     bit-exact with the reference.
 #include <cuda_fp16.h>
+
+#include <atomic>
+#include <vector>
 
 #include "common.cuh"
 
@@ -393,6 +398,307 @@ __global__ void chain_kernel(const __grid_constant__ ChainParams p,
     }
 }
 
+// ---- register-slot chain interpreter ---------------------------------------------
+// The interpreter above keeps every temp of an element in a 64-entry
+// per-thread array indexed at run time, so it lives in local memory, and it
+// streams one element per thread: ~10 % of HBM bandwidth on short chains.
+// This one keeps the temps in R registers (R = 4 or 8): on the host each
+// expression's result is given a slot by liveness (an SSA result's slot is
+// free again after its last reader), so a chain needs as many slots as it
+// has temps alive at once, and every operand names a constant, ElemA, ElemB
+// or a slot. Slot reads and writes are switches on a warp-uniform value whose
+// cases index the register array statically. Each thread evaluates 4
+// elements at a time, and its inputs arrive through a kChainStages-deep
+// cp.async pipeline into shared memory (each thread copies and reads only its
+// own elements, so no block barrier is needed), so the loads stay in flight
+// whatever the register count.
+constexpr int kChainThreads = 256;
+constexpr int kChainElems = 4;                       // elements per thread per tile
+constexpr int kChainTile = kChainThreads * kChainElems;
+constexpr int kChainStages = 4;
+
+// Operand sources: 0 constant, 1 ElemA, 2 ElemB, 3 + s register slot s.
+struct SlotExpr {
+    uint8_t op, asrc, bsrc, dst;
+    int32_t pad;
+    double aval, bval;
+};
+
+struct SlotChain {
+    int32_t n_exprs;
+    int32_t poly7;
+    int32_t out_slot;
+    int32_t uses_b;
+    SlotExpr e[kMaxExprs];
+};
+
+template <int R>
+__device__ __forceinline__ void fetch4(uint8_t src, double val, const double (&va)[4],
+                                       const double (&vb)[4], const double (&t)[R][4],
+                                       double (&x)[4]) {
+#define MLKB_SLOT_CASE(j)                                           \
+    case 3 + j:                                                     \
+        if constexpr (j < R) {                                      \
+            _Pragma("unroll") for (int q = 0; q < 4; ++q) x[q] = t[j][q]; \
+        }                                                           \
+        break;
+    switch (src) {
+        case 0:
+#pragma unroll
+            for (int q = 0; q < 4; ++q) x[q] = val;
+            break;
+        case 1:
+#pragma unroll
+            for (int q = 0; q < 4; ++q) x[q] = va[q];
+            break;
+        case 2:
+#pragma unroll
+            for (int q = 0; q < 4; ++q) x[q] = vb[q];
+            break;
+        MLKB_SLOT_CASE(0) MLKB_SLOT_CASE(1) MLKB_SLOT_CASE(2) MLKB_SLOT_CASE(3)
+        MLKB_SLOT_CASE(4) MLKB_SLOT_CASE(5) MLKB_SLOT_CASE(6) MLKB_SLOT_CASE(7)
+        default: break;
+    }
+#undef MLKB_SLOT_CASE
+}
+
+template <int R>
+__device__ __forceinline__ void put4(uint8_t dst, double (&t)[R][4], const double (&r)[4]) {
+#define MLKB_SLOT_PUT(j)                                            \
+    case j:                                                         \
+        if constexpr (j < R) {                                      \
+            _Pragma("unroll") for (int q = 0; q < 4; ++q) t[j][q] = r[q]; \
+        }                                                           \
+        break;
+    switch (dst) {
+        MLKB_SLOT_PUT(0) MLKB_SLOT_PUT(1) MLKB_SLOT_PUT(2) MLKB_SLOT_PUT(3)
+        MLKB_SLOT_PUT(4) MLKB_SLOT_PUT(5) MLKB_SLOT_PUT(6) MLKB_SLOT_PUT(7)
+        default: break;
+    }
+#undef MLKB_SLOT_PUT
+}
+
+// The operation of one expression over 4 elements; one switch per expression,
+// the same per-element arithmetic as apply<> (the reference's guards and
+// rounding; poly7 for Sin when asked).
+// The elementary functions, out of line: inlined four times into the
+// interpreter loop they would hold its registers (and occupancy) hostage.
+template <bool kF64Out>
+__device__ __noinline__ double apply_call(uint8_t op, double a, double b, int poly7) {
+    return apply<kF64Out>(op, a, b, poly7 != 0);
+}
+
+template <bool kF64Out>
+__device__ __forceinline__ void apply4(uint8_t op, const double (&x)[4], const double (&y)[4],
+                                       double (&r)[4], bool poly7) {
+#define MLKB_EACH(expr) _Pragma("unroll") for (int q = 0; q < 4; ++q) { const double a = x[q]; const double b = y[q]; (void)b; r[q] = (expr); } break;
+    switch (op) {
+        case kAdd: MLKB_EACH(__dadd_rn(a, b))
+        case kSub: MLKB_EACH(__dsub_rn(a, b))
+        case kMul: MLKB_EACH(__dmul_rn(a, b))
+        case kDiv: MLKB_EACH(b != 0.0 ? __ddiv_rn(a, b) : 0.0)
+        case kNeg: MLKB_EACH(-a)
+        default: MLKB_EACH((apply_call<kF64Out>(op, a, b, poly7 ? 1 : 0)))
+    }
+#undef MLKB_EACH
+}
+
+template <typename T>
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+                 "l"(src), "r"(bytes)
+                 : "memory");
+}
+
+template <typename T, int R>
+__global__ void __launch_bounds__(kChainThreads)
+chain_tile_kernel(const __grid_constant__ SlotChain p, const T* __restrict__ a,
+                  const T* __restrict__ b, T* __restrict__ out, int64_t n) {
+    extern __shared__ __align__(16) uint8_t chain_smem[];
+    // [stage][input][kChainTile] elements of T
+    T* const tiles_smem = reinterpret_cast<T*>(chain_smem);
+    const int inputs = p.uses_b ? 2 : 1;
+    const int64_t tiles = (n + kChainTile - 1) / kChainTile;
+    const int tid = static_cast<int>(threadIdx.x);
+    constexpr int kChunks = kChainElems * static_cast<int>(sizeof(T)) / 16;  // 16 B copies per input
+    constexpr int kPerChunk = 16 / static_cast<int>(sizeof(T));
+    auto slot_ptr = [&](int stage, int input) {
+        return tiles_smem + (static_cast<size_t>(stage) * inputs + input) * kChainTile +
+               static_cast<size_t>(tid) * kChainElems;
+    };
+    // Copies this thread's elements of `tile` (zero past n) into `stage`.
+    auto issue = [&](int64_t tile, int stage) {
+        if (tile < tiles) {
+            const int64_t base = tile * kChainTile + static_cast<int64_t>(tid) * kChainElems;
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) {
+                const int64_t e0 = base + c * kPerChunk;
+                const int64_t left = n - e0;
+                const uint32_t bytes =
+                    left <= 0 ? 0u
+                              : static_cast<uint32_t>((left < kPerChunk ? left : kPerChunk) *
+                                                      static_cast<int64_t>(sizeof(T)));
+                const int64_t src = bytes != 0 ? e0 : 0;  // no byte is read when bytes == 0
+                cp_async16<T>(slot_ptr(stage, 0) + c * kPerChunk, a + src, bytes);
+                if (p.uses_b) cp_async16<T>(slot_ptr(stage, 1) + c * kPerChunk, b + src, bytes);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    const int64_t g = gridDim.x;
+    int64_t tile = blockIdx.x;
+#pragma unroll
+    for (int st = 0; st < kChainStages - 1; ++st) issue(tile + st * g, st);
+    for (int it = 0; tile < tiles; ++it, tile += g) {
+        const int stage = it % kChainStages;
+        asm volatile("cp.async.wait_group %0;" ::"n"(kChainStages - 2) : "memory");
+        double va[4], vb[4];
+        const T* sa = slot_ptr(stage, 0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) va[q] = static_cast<double>(sa[q]);
+        if (p.uses_b) {
+            const T* sb = slot_ptr(stage, 1);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) vb[q] = static_cast<double>(sb[q]);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) vb[q] = 0.0;
+        }
+        // the stage read above is free: refill it with the tile S-1 ahead
+        issue(tile + (kChainStages - 1) * g, (it + kChainStages - 1) % kChainStages);
+        double t[R][4];  // every slot is written before it is read (allocateSlots)
+        for (int k = 0; k < p.n_exprs; ++k) {
+            const SlotExpr& e = p.e[k];
+            double x[4], y[4], r[4];
+            fetch4<R>(e.asrc, e.aval, va, vb, t, x);
+            fetch4<R>(e.bsrc, e.bval, va, vb, t, y);
+            apply4<sizeof(T) == 8>(e.op, x, y, r, p.poly7 != 0);
+            put4<R>(e.dst, t, r);
+        }
+        double res[4];
+        fetch4<R>(static_cast<uint8_t>(3 + p.out_slot), 0.0, va, vb, t, res);
+        const int64_t base = tile * kChainTile + static_cast<int64_t>(tid) * kChainElems;
+        if (base + kChainElems <= n) {
+            if constexpr (sizeof(T) == 4) {
+                *reinterpret_cast<float4*>(out + base) =
+                    make_float4(static_cast<float>(res[0]), static_cast<float>(res[1]),
+                                static_cast<float>(res[2]), static_cast<float>(res[3]));
+            } else {
+                reinterpret_cast<double2*>(out + base)[0] = make_double2(res[0], res[1]);
+                reinterpret_cast<double2*>(out + base)[1] = make_double2(res[2], res[3]);
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (base + q < n) out[base + q] = static_cast<T>(res[q]);
+            }
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+template <typename T, int R>
+int launchChainTile(const SlotChain& sc, const void* a, const void* b, void* out, int64_t n,
+                    cudaStream_t s) {
+    const size_t smem = static_cast<size_t>(kChainStages) * (sc.uses_b ? 2 : 1) * kChainTile *
+                        sizeof(T);
+    static std::atomic<int> blocksPerSm[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int per = dev >= 0 && dev < 64 ? blocksPerSm[dev].load() : 0;
+    if (per == 0) {
+        cudaError_t e = cudaFuncSetAttribute(chain_tile_kernel<T, R>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kChainStages * 2 * kChainTile *
+                                                              sizeof(T)));
+        if (e != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, e, "chain smem attribute");
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, chain_tile_kernel<T, R>,
+                                                          kChainThreads, smem);
+        if (e != cudaSuccess || per <= 0) per = 1;
+        if (dev >= 0 && dev < 64) blocksPerSm[dev] = per;
+    }
+    const int64_t tiles = (n + kChainTile - 1) / kChainTile;
+    const int64_t cap = static_cast<int64_t>(smCount()) * per;
+    const int grid = static_cast<int>(tiles < cap ? tiles : cap);
+    chain_tile_kernel<T, R><<<grid, kChainThreads, smem, s>>>(
+        sc, static_cast<const T*>(a), static_cast<const T*>(b), static_cast<T*>(out), n);
+    return checkLaunch("chain kernel launch");
+}
+
+// Slots for a chain by liveness: returns the slot count, or -1 when the
+// chain needs more than `limit` (or has an operand of another kind).
+int allocateSlots(const DevExpr* ex, int n, int limit, SlotChain& sc) {
+    std::vector<int> last(static_cast<size_t>(n), -1);
+    for (int k = 0; k < n; ++k) {
+        for (int side = 0; side < 2; ++side) {
+            if (side == 1 && ex[k].unary) break;
+            if ((side == 0 ? ex[k].akind : ex[k].bkind) == kTemp) {
+                last[static_cast<size_t>(side == 0 ? ex[k].aidx : ex[k].bidx)] = k;
+            }
+        }
+    }
+    last[static_cast<size_t>(n - 1)] = n;  // the chain's result
+    std::vector<int> slotOf(static_cast<size_t>(n), -1);
+    std::vector<int> freeSlots;
+    int used = 0;
+    for (int k = 0; k < n; ++k) {
+        SlotExpr& e = sc.e[k];
+        e.op = ex[k].op;
+        for (int side = 0; side < 2; ++side) {
+            uint8_t kind = side == 0 ? ex[k].akind : ex[k].bkind;
+            double val = side == 0 ? ex[k].aval : ex[k].bval;
+            const int idx = side == 0 ? ex[k].aidx : ex[k].bidx;
+            uint8_t src = 0;
+            if (side == 1 && ex[k].unary) {
+                src = 0;
+                val = 0.0;
+            } else if (kind == kConst) {
+                src = 0;
+            } else if (kind == kElemA) {
+                src = 1;
+            } else if (kind == kElemB) {
+                src = 2;
+            } else if (kind == kTemp) {
+                src = static_cast<uint8_t>(3 + slotOf[static_cast<size_t>(idx)]);
+            } else {
+                return -1;
+            }
+            (side == 0 ? e.asrc : e.bsrc) = src;
+            (side == 0 ? e.aval : e.bval) = val;
+        }
+        // Operands read for the last time here free their slots before this
+        // result takes one (operands are read before the result is written).
+        for (int side = 0; side < 2; ++side) {
+            if (side == 1 && ex[k].unary) break;
+            if ((side == 0 ? ex[k].akind : ex[k].bkind) != kTemp) continue;
+            const int idx = side == 0 ? ex[k].aidx : ex[k].bidx;
+            if (last[static_cast<size_t>(idx)] == k && slotOf[static_cast<size_t>(idx)] >= 0) {
+                freeSlots.push_back(slotOf[static_cast<size_t>(idx)]);
+                slotOf[static_cast<size_t>(idx)] = -2;  // released (both operands may name it)
+            }
+        }
+        int slot;
+        if (!freeSlots.empty()) {
+            slot = freeSlots.back();
+            freeSlots.pop_back();
+        } else {
+            slot = used++;
+        }
+        if (used > limit) return -1;
+        slotOf[static_cast<size_t>(k)] = slot;
+        e.dst = static_cast<uint8_t>(slot);
+        if (last[static_cast<size_t>(k)] < 0) {  // never read: free at once
+            freeSlots.push_back(slot);
+            slotOf[static_cast<size_t>(k)] = -2;
+        }
+    }
+    sc.n_exprs = n;
+    sc.out_slot = slotOf[static_cast<size_t>(n - 1)] >= 0 ? slotOf[static_cast<size_t>(n - 1)]
+                                                          : sc.e[n - 1].dst;
+    return used;
+}
+
 }  // namespace
 
 bool isUnaryOp(int op) {
@@ -479,6 +785,29 @@ extern "C" int mlkb_map_chain(const mlkb_expr* exprs, int32_t n_exprs, int32_t p
         }
     }
     cudaStream_t s = asStream(stream);
+    // The register-slot interpreter when the chain fits 8 slots and every
+    // buffer is 16-byte aligned (cp.async and vector stores); else the
+    // local-array interpreter below.
+    const bool aligned = aligned16(a) && aligned16(out) && (b == nullptr || aligned16(b));
+    if (aligned && a != nullptr) {
+        SlotChain sc{};
+        sc.poly7 = p.poly7;
+        const int used = allocateSlots(p.e, n_exprs, 8, sc);
+        if (used > 0) {
+            bool uses_b = false;
+            for (int k = 0; k < n_exprs; ++k) {
+                uses_b = uses_b || sc.e[k].asrc == 2 || sc.e[k].bsrc == 2;
+            }
+            if (uses_b && b == nullptr) return setError(MLKB_ERR_INVALID, "chain: ElemB read but no B buffer");
+            sc.uses_b = uses_b ? 1 : 0;
+            if (elem_dtype == MLKB_F32) {
+                return used <= 4 ? launchChainTile<float, 4>(sc, a, b, out, n, s)
+                                 : launchChainTile<float, 8>(sc, a, b, out, n, s);
+            }
+            return used <= 4 ? launchChainTile<double, 4>(sc, a, b, out, n, s)
+                             : launchChainTile<double, 8>(sc, a, b, out, n, s);
+        }
+    }
     const int grid = gridFor(n, 256);
     if (elem_dtype == MLKB_F32) {
         chain_kernel<float><<<grid, 256, 0, s>>>(p,

@@ -138,3 +138,50 @@ def test_roots_with_their_own_static_ranges(cuda):
     (r0,) = oracle.port().chain([kir.SIN_CHAIN], xh.astype(np.float64))
     assert oracle.ulp_f32(y0, r0).max() <= 2
     assert np.array_equal(y1, xh[:500] * 2)
+
+
+def _wide_chain(live):
+    """`live` products of x kept alive at once, then summed: needs `live` + 1
+    register slots (or the local-array interpreter past 8)."""
+    A, C, T, E = kir.A, kir.C, kir.T, kir.E
+    ex = [E("mul", A, C(1.0 + 0.5 * j)) for j in range(live)]
+    acc = len(ex)
+    ex.append(E("add", T(0), T(1)))
+    for j in range(2, live):
+        ex.append(E("add", T(len(ex) - 1), T(j)))
+    ex.append(E("mul", T(len(ex) - 1), A))        # reads x once more
+    ex.append(E("exp", C(0.0)))                    # a dead result (never read)
+    ex.append(E("sub", T(len(ex) - 2), C(0.25)))
+    return kir.chain(*ex)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("live", [2, 6, 11])
+def test_chain_slot_allocation_paths(cuda, dtype, live):
+    # 2 live temps: 4 register slots; 6: 8 slots; 11: the local-array
+    # interpreter. Arithmetic chains are bit-exact in f64 and round once to
+    # f32, so both dtypes must equal the oracle exactly.
+    ch = _wide_chain(live)
+    xh = np.linspace(-3, 3, 100003).astype(dtype)
+    (want,) = oracle.port().chain([ch], xh.astype(np.float64))
+    for off in (0, 1):                               # 1: unaligned -> the fallback
+        x = dev(cuda, xh)[off:]
+        y = empty(cuda, (xh.size,), cuda.float64 if dtype == np.float64 else cuda.float32)[off:]
+        api.map_chain(ch, x, y)
+        got = host(y).astype(np.float64)
+        assert np.array_equal(got, want[off:].astype(dtype).astype(np.float64)), (live, off)
+
+
+def test_chain_two_inputs_and_tail(cuda):
+    # ElemA and ElemB through the staged loads, lengths around a tile edge
+    ch = kir.chain(kir.E("mul", kir.A, kir.B), kir.E("div", kir.T(0), kir.B),
+                   kir.E("add", kir.T(1), kir.A))
+    for n in (1, 4, 1023, 1024, 1025, 4096 * 3 + 3):
+        rng = np.random.default_rng(n)
+        ah = rng.normal(0, 2, n)
+        bh = rng.normal(0, 2, n)
+        bh[::7] = 0.0                                 # Div by 0 -> 0
+        y = empty(cuda, (n,), cuda.float64)
+        api.map_chain(ch, dev(cuda, ah), y, b=dev(cuda, bh))
+        (want,) = oracle.port().chain([ch], ah, bh)
+        assert np.array_equal(host(y), want), n

@@ -559,6 +559,7 @@ def strong_configs(torch, api, mdist, args, dist, world, rank, peaks):
     hbm, tc = peaks["hbm_gbs"], peaks["bf16_tflops"]
 
     def rec(name, fn, work, unit, peak):
+        time.sleep(1.0)  # from an idle GPU, like the weak-scaling configs (a burst)
         sec = time_device(torch, fn, args.warmup, args.steps, dist, world)
         scale = 1e9 if unit == "GB/s" else 1e12
         out[name] = {"value": work / sec / scale, "unit": unit, "ms": sec * 1e3,

@@ -44,6 +44,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cmath>
 #include <cstdio>
 
 #include "common.cuh"
@@ -60,7 +61,7 @@ namespace {
 constexpr int kRows = 128;   // score rows per unit (M of the MMA)
 constexpr int kChunk = 128;  // score columns per accumulator (N of the MMA)
 constexpr int kKStages = 5;  // K ring depth, [128 x 64] f16 boxes
-constexpr int kRun = 4;      // consecutive bands of one batch per CTA
+constexpr int kRun = 4;      // longest run of consecutive bands of one batch per CTA
 constexpr int kQSlots = 3;   // Q bands resident: units i-1, i and the prefetched i+1
 constexpr uint32_t kKBox = kChunk * 64 * 2;  // 16 KB
 constexpr uint32_t kQBox = kRows * 64 * 2;   // 16 KB (one d-half)
@@ -108,7 +109,7 @@ template <int kS, bool kKt>
 __global__ void __launch_bounds__(kThreads, 1)
 qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k, float* __restrict__ y, int batch,
-                   int m, int s_in, int d, float c2, int* __restrict__ status) {
+                   int m, int s_in, int d, int run, float c2, int* __restrict__ status) {
     const int s = kS != 0 ? kS : s_in;  // row length, a constant where specialised
     // The kernel has no static shared memory, so the dynamic window starts at
     // the 1024-byte aligned base the 128B-swizzled tiles need.
@@ -123,11 +124,11 @@ qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
     const int units = batch * bands;
     const int chunks = s / kChunk;
     const int dh = d / 64;  // d-halves (1 or 2)
-    // This CTA's units: runs of kRun consecutive bands of one batch, the runs
+    // This CTA's units: runs of `run` consecutive bands of one batch (run
+    // divides bands; chosen on the host), the runs
     // dealt round-robin over the CTAs. Within a run pass 2 of unit i-1 and
     // pass 1 of unit i read the same K (one load feeds both), while the CTAs
     // together stay on a few batches at a time, so K and Q stay L2-resident.
-    const int run = (bands % kRun == 0) ? kRun : 1;
     const int runs = units / run;
     const int nruns = runs > static_cast<int>(blockIdx.x)
                           ? (runs - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
@@ -551,11 +552,32 @@ int launchQkSoftmax(const void* q, const void* k, float* y, int64_t batch, int64
     }
     const int64_t units = batch * (m / kRows);
     const int grid = static_cast<int>(units < smCount() ? units : smCount());
+    // Run length: the longest of 4, 2, 1 bands that divides a batch's bands
+    // and keeps the last wave of runs over the CTAs at least as full as any
+    // shorter run would (within 2 %). Longer runs share K loads and keep the
+    // CTAs on few batches at a time (K stays in L2); shorter runs balance
+    // better when few units remain (a batch split over several GPUs).
+    const int64_t bands = m / kRows;
+    int run = 1;
+    double best = 0.0;
+    for (int r = kRun; r >= 1; r /= 2) {
+        if (bands % r != 0) continue;
+        const double runs = static_cast<double>(units / r);
+        const double waves = std::ceil(runs / grid);
+        const double fill = runs / (waves * grid);
+        if (run == 1 && best == 0.0) {
+            run = r;
+            best = fill;
+        } else if (fill > best + 0.02) {
+            run = r;
+            best = fill;
+        }
+    }
     // exp(scale * v) = exp2(scale * log2(e) * v)
     const float c2 = static_cast<float>(scale * 1.4426950408889634);
     kern<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, y, static_cast<int>(batch),
                                              static_cast<int>(m), static_cast<int>(s),
-                                             static_cast<int>(d), c2, deviceStatusPtr());
+                                             static_cast<int>(d), run, c2, deviceStatusPtr());
     const cudaError_t le = cudaGetLastError();
     if (le != cudaSuccess) {
         cudaFuncAttributes fa{};

@@ -109,8 +109,11 @@ template <int kS, bool kKt>
 __global__ void __launch_bounds__(kThreads, 1)
 qk_softmax_tcgen05(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k, float* __restrict__ y, int batch,
-                   int m, int s_in, int d, int run, float c2, int* __restrict__ status) {
-    const int s = kS != 0 ? kS : s_in;  // row length, a constant where specialised
+                   int m_in, int s_in, int d, int run, float c2, int* __restrict__ status) {
+    // Row length (keys) and rows per batch: constants in the instances
+    // specialised on square batches (m == s), run-time values otherwise.
+    const int s = kS != 0 ? kS : s_in;
+    const int m = kS != 0 ? kS : m_in;
     // The kernel has no static shared memory, so the dynamic window starts at
     // the 1024-byte aligned base the 128B-swizzled tiles need.
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -532,10 +535,11 @@ int launchQkSoftmax(const void* q, const void* k, float* y, int64_t batch, int64
                  kSmemBytes, optin);
         return setError(MLKB_ERR_LAUNCH, msg);
     }
-    // Row lengths of 1024, 2048 and 4096 get a kernel specialised on them: a
-    // pass-2 warp then addresses all 32 rows of a group from one base by
-    // immediate offsets instead of stepping a 64-bit pointer per store.
-    const int len = s == 1024 ? 1 : s == 2048 ? 2 : s == 4096 ? 3 : 0;
+    // Square batches (m == s) with row lengths of 1024, 2048 and 4096 get a
+    // kernel specialised on them: a pass-2 warp then addresses all 32 rows of
+    // a group from one base by immediate offsets instead of stepping a 64-bit
+    // pointer per store.
+    const int len = m != s ? 0 : s == 1024 ? 1 : s == 2048 ? 2 : s == 4096 ? 3 : 0;
     using Kern = decltype(&qk_softmax_tcgen05<0, false>);
     static const Kern kKerns[8] = {
         qk_softmax_tcgen05<0, false>,    qk_softmax_tcgen05<1024, false>,

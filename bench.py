@@ -190,6 +190,17 @@ def cpu_reference_configs(reps: int = 3):
     out["map1"] = {"value": n1 * 8 / t / 1e9, "unit": "GB/s", "cores": thr, "kind": kind,
                    "sample": "the full 2^24-element config 1, f64 arithmetic, bytes at f32 "
                              "width (8 B/element)"}
+    # the generic chain row: the pipeline's derivative chain on 2^24 of 2^28
+    import json as _json
+
+    pipe = np.load(os.path.join(ROOT, "tests", "golden", "pipeline.npz"))
+    dchain = kir.chains_of(_json.loads(str(pipe["dsin_json"])))[-1]
+    xc = oracle.fill_uniform_f32(n1, SEED, 7, -8.0, 8.0).astype(np.float64)
+    t = timed(lambda: ex.chain([dchain], xc, threads=thr))
+    out["chain"] = {"value": n1 * 8 / t / 1e9, "unit": "GB/s", "cores": thr, "kind": kind,
+                    "sample": "2^24 of the 2^28 elements, the pipeline's derivative chain, "
+                              "f64 arithmetic, bytes at f32 width (8 B/element)"}
+    del xc
     # config 3: 1024 of the 65536 rows (Call(Softmax) is single-threaded)
     xs = (rng.standard_normal((1024, 4096)) * 4.0).astype(np.float32).astype(np.float64)
     t = timed(lambda: ex.softmax(xs))
@@ -735,6 +746,33 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
         {"note": "steps rotate over 8 input/output pairs (1 GiB > L2), no flush",
          "parity": g1})
     del xs1, ys1
+
+    # the generic chain path: the derivative chain the
+    # reference's calculus passes emit for config 2 (Tier-1 output committed in
+    # tests/golden/pipeline.npz), 2^28 f32 through mlkb_map_chain, which runs
+    # it as a chain kernel compiled at run time (no dedicated kernel applies
+    # on this entry). 8 B per element; 2 GiB touched per step (> L2).
+    import numpy as _np
+
+    from mlk2_b200 import kir
+
+    pipe = _np.load(os.path.join(ROOT, "tests", "golden", "pipeline.npz"))
+    dchain = kir.chains_of(json.loads(str(pipe["dsin_json"])))[-1]
+    nc = 1 << 28
+    xc = torch.empty(nc, device="cuda")
+    api.fill(xc, SEED, 7 + 256 * rank, "uniform", -8.0, 8.0)
+    yc = torch.empty_like(xc)
+    _, _, launched0 = api.chain_compile(-1)
+    api.map_chain(dchain, xc, yc)
+    xs64 = xc[::4096].double()
+    gc = parity_gate(torch, "pipeline d/dx sin(x^2+3x) via the generic chain", yc[::4096],
+                     torch.cos(xs64 * xs64 + 3.0 * xs64) * (2.0 * xs64 + 3.0), ulp_bound=2)
+    active, _, launched1 = api.chain_compile(-1)
+    sec = measure(lambda: api.map_chain(dchain, xc, yc))
+    rec("chain", sec, nc * 8, "GB/s", "hbm", peaks["hbm_gbs"], 1,
+        {"parity": gc, "path": "compiled" if active and launched1 > launched0 else "interpreted",
+         "kernel": "mlkb_chain_kernel (NVRTC, run time)"})
+    del xc, yc
 
     # config 3: softmax [65536 x 4096] f32 per GPU
     xs = torch.empty((65536, 4096), device="cuda")

@@ -258,11 +258,35 @@ int mlkb_map_sin_dsin_f32(const float* x, float* y, float* dy, int64_t n,
  * poly7_sin != 0 evaluates Sin with the reference's "poly7" family,
  * families::polySin (compiler/include/mlk/support/math_families.h:81-90),
  * bit-identical to it in f64; other ops keep the libm family
- * (kernel_buffers.cpp:42-51). */
+ * (kernel_buffers.cpp:42-51).
+ * The first call for a chain STRUCTURE (ops, operand kinds and temp indices,
+ * poly7, dtype, whether b is read) compiles a straight-line kernel for it
+ * with NVRTC, in-process, and caches it; constants and scalars are kernel
+ * parameters, so other values reuse it. Where NVRTC cannot be loaded
+ * (MLKB_NVRTC_LIB names the library, default libnvrtc.so.12), or
+ * compilation is off (mlkb_chain_compile), an interpreter kernel runs the
+ * chain instead, with identical results. */
 int mlkb_map_chain(const mlkb_expr* exprs, int32_t n_exprs, int32_t poly7_sin,
                    const void* a, const void* b, void* out, int32_t elem_dtype,
                    int64_t n, const double* scalars, int64_t n_scalars,
                    void* stream);
+
+/* Run-time compilation of chains. mode 1 compiles chains on first use (the
+ * default; MLKB_CHAIN_JIT=0 in the environment starts the process at 0),
+ * 0 runs every chain on the interpreter, any other value changes nothing.
+ * Returns 1 when chains will be compiled (mode 1 and NVRTC loadable), else 0;
+ * *compiled and *launched (either may be NULL) receive how many chain
+ * kernels this process has compiled and launched. No counterpart in the
+ * reference (its chains are compiled by an out-of-process nvcc). */
+int32_t mlkb_chain_compile(int32_t mode, int64_t* compiled, int64_t* launched);
+
+/* Compiles and caches the kernel mlkb_map_chain would use for this chain
+ * structure without launching anything (no GPU needed): MLKB_OK, or
+ * MLKB_ERR_UNSUPPORTED with the NVRTC log's head in mlkb_last_error() when
+ * it cannot be compiled (the interpreter then runs the chain). has_b: the
+ * call will pass a b buffer. */
+int mlkb_chain_build(const mlkb_expr* exprs, int32_t n_exprs, int32_t poly7_sin,
+                     int32_t elem_dtype, int32_t has_b);
 
 /* Row softmax Y[m,:] = softmax(X[m,:]) over a row-major [rows, cols] matrix
  * (reference execSoftmaxCall, kernel_buffers.cpp:290-340). */

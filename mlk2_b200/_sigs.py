@@ -27,6 +27,8 @@ SIGNATURES = {
     "mlkb_map_sin_f32": (i32, [vp, vp, i64, vp]),
     "mlkb_map_sin_dsin_f32": (i32, [vp, vp, vp, i64, vp]),
     "mlkb_map_chain": (i32, [vp, i32, i32, vp, vp, vp, i32, i64, C.POINTER(f64), i64, vp]),
+    "mlkb_chain_compile": (i32, [i32, C.POINTER(i64), C.POINTER(i64)]),
+    "mlkb_chain_build": (i32, [vp, i32, i32, i32, i32]),
     "mlkb_softmax_f32": (i32, [vp, vp, i64, i64, vp]),
     "mlkb_softmax_f64": (i32, [vp, vp, i64, i64, vp]),
     "mlkb_softmax_f32_noalloc": (i32, [vp, vp, i64, i64, i32, vp]),

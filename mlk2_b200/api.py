@@ -69,6 +69,22 @@ def map_chain(exprs: np.ndarray, a, out, b=None, scalars: Sequence[float] = (), 
                                _stream(stream)))
 
 
+def chain_compile(mode: int = -1):
+    """Run-time chain compilation: mode 1 on, 0 off (interpreter), -1 query.
+    Returns (active, compiled, launched): whether chains will be compiled and
+    how many chain kernels this process has compiled and launched."""
+    comp, launched = C.c_int64(0), C.c_int64(0)
+    active = lib().mlkb_chain_compile(int(mode), C.byref(comp), C.byref(launched))
+    return bool(active), comp.value, launched.value
+
+
+def chain_build(exprs: np.ndarray, dtype: str = "f32", has_b: bool = False, poly7=False):
+    """Compiles the kernel map_chain would use for this chain (no GPU needed)."""
+    exprs = np.ascontiguousarray(exprs, dtype=kir.EXPR_DTYPE)
+    check(lib().mlkb_chain_build(exprs.ctypes.data, len(exprs), int(poly7),
+                                 F64 if dtype == "f64" else F32, int(has_b)))
+
+
 def softmax(x, y, stream=None):
     rows, cols = x.shape
     fn = lib().mlkb_softmax_f32 if _dt_of(x) == F32 else lib().mlkb_softmax_f64

@@ -27,6 +27,25 @@ int smCount();
 // mlkb_take_device_error() reads and clears it. nullptr if allocation failed.
 int* deviceStatusPtr();
 
+// One chain expression for the run-time compiled chain kernels
+// (chain_jit.cpp): op and operand kinds as in mlkb_expr, ScalarParam
+// operands already resolved to constants (kind kConst), temps as indices of
+// earlier expressions.
+struct JitExpr {
+    int op, akind, bkind, unary, aidx, bidx;
+    double aval, bval;
+};
+// Returned by the two calls below when the chain was not compiled (NVRTC
+// absent, compilation switched off, or it failed): the caller interprets it.
+constexpr int kJitUnavailable = -100;
+// Runs the chain over n elements of a (and b) into out (dtype MLKB_F32 or
+// MLKB_F64) as a compiled straight-line kernel, compiling it on first use.
+int launchChainJit(const JitExpr* e, int n_exprs, bool poly7, const void* a, const void* b,
+                   void* out, int dtype, int64_t n, cudaStream_t s);
+// Compiles (and caches) the chain's kernel without launching it; *why gets
+// the reason when it returns kJitUnavailable.
+int buildChainJit(const JitExpr* e, int n_exprs, bool poly7, int dtype, const char** why);
+
 // Scaled-scores softmax Y[b] = softmax_rows(scale * Q[b] K[b]^T), Q [batch, m,
 // d] f16; K given as [batch, s, d] (kt false) or as Kt [batch, d, s] (kt
 // true); Y [batch, m, s] f32 (qk_softmax.cu).
@@ -45,106 +64,5 @@ inline bool aligned16(const void* p) {
 
 }  // namespace mlkb
 
-// ---- device math helpers ----------------------------------------------------
-namespace mlkb::dev {
 
-// f64 argument reduction by pi/2 for |u| < 2^20 (Cody-Waite, two-term
-// constant, FMA). r1 = u - k*P1 is exact (both terms are multiples of 2^-52
-// or finer and |r1| < 1 fits in 53 bits); the second term carries pi/2 - P1.
-// Returns k mod 4 in q.
-__device__ __forceinline__ double reduce_pio2(double u, int& q) {
-    const double kTwoOverPi = 0.6366197723675814;   // fl64(2/pi)
-    const double kP1 = 1.5707963267948966;            // fl64(pi/2)
-    const double kP2 = 6.123233995736766e-17;           // fl64(pi/2 - kP1)
-    const double kMagic = 6755399441055744.0;            // 1.5 * 2^52
-    const double t = fma(u, kTwoOverPi, kMagic);
-    const double kd = t - kMagic;
-    q = __double2loint(t);
-    const double r1 = fma(-kd, kP1, u);
-    return fma(-kd, kP2, r1);
-}
-
-// sin and cos of the reduced argument |r| <= pi/4 (+ a rounding margin),
-// Taylor series through r^11 (sin) and r^12 (cos), Horner form in f64.
-// Truncation error < 1e-11 relative, far below f32 resolution.
-__device__ __forceinline__ double sin_poly(double r, double z) {
-    double p = -2.505210838544172e-08;   // -1/11!
-    p = fma(z, p, 2.7557319223985893e-06);  // 1/9!
-    p = fma(z, p, -1.984126984126984e-04); // -1/7!
-    p = fma(z, p, 8.333333333333333e-03);  // 1/5!
-    p = fma(z, p, -1.6666666666666666e-01); // -1/3!
-    return fma(r * z, p, r);
-}
-
-__device__ __forceinline__ double cos_poly(double z) {
-    double p = 2.08767569878681e-09;     // 1/12!
-    p = fma(z, p, -2.755731922398589e-07);  // -1/10!
-    p = fma(z, p, 2.48015873015873e-05);   // 1/8!
-    p = fma(z, p, -1.388888888888889e-03);  // -1/6!
-    p = fma(z, p, 4.1666666666666664e-02);   // 1/4!
-    p = fma(z, p, -0.5);
-    return fma(z, p, 1.0);
-}
-
-// sin(u), cos(u) in f64 for any u: the reduction above for |u| < 2^20,
-// CUDA's own sincos otherwise (and for NaN / inf).
-__device__ __forceinline__ void sincos_f64(double u, double& s, double& c) {
-    if (fabs(u) < 1048576.0) {
-        int q;
-        const double r = reduce_pio2(u, q);
-        const double z = r * r;
-        const double sr = sin_poly(r, z);
-        const double cr = cos_poly(z);
-        // quadrant q: (sin, cos) = (sr, cr), (cr, -sr), (-sr, -cr), (-cr, sr)
-        const double a = (q & 1) ? cr : sr;
-        const double b = (q & 1) ? sr : cr;
-        s = (q & 2) ? -a : a;
-        c = ((q + 1) & 2) ? -b : b;
-    } else {
-        ::sincos(u, &s, &c);
-    }
-}
-
-__device__ __forceinline__ double sin_f64(double u) {
-    if (fabs(u) < 1048576.0) {
-        int q;
-        const double r = reduce_pio2(u, q);
-        const double z = r * r;
-        const double v = (q & 1) ? cos_poly(z) : sin_poly(r, z);
-        return (q & 2) ? -v : v;
-    }
-    return ::sin(u);
-}
-
-// exp(d) in f64 for d <= 0 (softmax exponents). Values below -120 return 0:
-// they lie under half the smallest f32 subnormal times any row sum >= 1, and
-// add nothing to an f64 sum >= 1. NaN propagates; -inf gives 0.
-// Method: k = rint(d/ln2) by the 1.5*2^52 shifter, r = d - k*ln2 with a
-// two-term ln2 (the first product is exact under FMA), Taylor series of e^r
-// through r^8 on |r| <= ln2/2 (truncation < 3e-10 relative), scale by 2^k.
-__device__ __forceinline__ double exp_neg_f64(double d) {
-    if (!(d >= -120.0)) return (d != d) ? d : 0.0;
-    const double kLog2e = 1.4426950408889634;
-    const double kLn2Hi = 0.6931471805599453;    // fl64(ln 2)
-    const double kLn2Lo = 2.3190468138462996e-17;  // fl64(ln 2 - kLn2Hi)
-    const double kMagic = 6755399441055744.0;
-    const double t = fma(d, kLog2e, kMagic);
-    const double kd = t - kMagic;
-    const int k = __double2loint(t);
-    double r = fma(-kd, kLn2Hi, d);
-    r = fma(-kd, kLn2Lo, r);
-    double p = 2.48015873015873e-05;     // 1/8!
-    p = fma(r, p, 1.984126984126984e-04);   // 1/7!
-    p = fma(r, p, 1.388888888888889e-03);   // 1/6!
-    p = fma(r, p, 8.333333333333333e-03);   // 1/5!
-    p = fma(r, p, 4.1666666666666664e-02);   // 1/4!
-    p = fma(r, p, 1.6666666666666666e-01);   // 1/3!
-    p = fma(r, p, 0.5);
-    p = fma(r, p, 1.0);
-    p = fma(r, p, 1.0);
-    // 2^k for -175 <= k <= 1 is a normal double: build its bit pattern.
-    const double scale = __hiloint2double((k + 1023) << 20, 0);
-    return p * scale;
-}
-
-}  // namespace mlkb::dev
+#include "chain_math.cuh"

@@ -251,12 +251,7 @@ int launchMap(const float* x, float* y0, float* y1, int64_t n, void* stream) {
 
 // ---- generic chain interpreter ---------------------------------------------
 
-// MathOp / KernelOperand::Kind numbering (include/mlkb200.h).
-enum : uint8_t {
-    kAdd = 0, kSub, kMul, kDiv, kNeg, kPow, kExp, kLog, kSin, kCos, kTan,
-    kTanh, kSqrt, kRsqrt, kErf, kGelu
-};
-enum : uint8_t { kConst = 0, kElemA, kElemB, kScalar, kTemp };
+using namespace chain;  // op and operand numbering, poly7, apply<> (chain_math.cuh)
 
 constexpr int kMaxExprs = 64;
 
@@ -276,96 +271,6 @@ struct ChainParams {
     int32_t poly7;
     DevExpr e[kMaxExprs];
 };
-
-// The reference's "poly7" sine family, families::polySin
-// (compiler/include/mlk/support/math_families.h:22-90): Cody-Waite reduction
-// by pi/2 = hi + lo, then a degree-13 odd sine or degree-12 even cosine
-// residual polynomial on [-pi/4, pi/4] picked by the quadrant. The reference
-// evaluates it in plain IEEE f64 without contraction; every step here is the
-// same correctly rounded operation in the same order (__d*_rn, no FMA), so
-// the result is bit-identical. The coefficients are the reference's own
-// published constants (math_families.h:30-35, :49-54).
-__device__ __forceinline__ double poly7_sin_reduced(double x) {
-    const double r2 = __dmul_rn(x, x);
-    double p = 1.58962301576546568060e-10;
-    p = __dadd_rn(__dmul_rn(p, r2), -2.50507477628578072866e-8);
-    p = __dadd_rn(__dmul_rn(p, r2), 2.75573136213857245213e-6);
-    p = __dadd_rn(__dmul_rn(p, r2), -1.98412698295895385996e-4);
-    p = __dadd_rn(__dmul_rn(p, r2), 8.33333333332211858878e-3);
-    p = __dadd_rn(__dmul_rn(p, r2), -1.66666666666666307295e-1);
-    return __dadd_rn(x, __dmul_rn(__dmul_rn(x, r2), p));  // x + x*r2*p, left to right
-}
-
-__device__ __forceinline__ double poly7_cos_reduced(double x) {
-    const double r2 = __dmul_rn(x, x);
-    double p = -1.13585365213876817300e-11;
-    p = __dadd_rn(__dmul_rn(p, r2), 2.08757530072652689750e-9);
-    p = __dadd_rn(__dmul_rn(p, r2), -2.75573142103085808917e-7);
-    p = __dadd_rn(__dmul_rn(p, r2), 2.48015872890001867312e-5);
-    p = __dadd_rn(__dmul_rn(p, r2), -1.38888888888783992457e-3);
-    p = __dadd_rn(__dmul_rn(p, r2), 4.16666666666666435770e-2);
-    // 1 - r2*0.5 + r2*r2*p, left to right
-    return __dadd_rn(__dsub_rn(1.0, __dmul_rn(r2, 0.5)), __dmul_rn(__dmul_rn(r2, r2), p));
-}
-
-__device__ __forceinline__ double poly7_sin(double x) {
-    const double kPio2Hi = 1.5707963267948965580e+00;  // also the reference's kPiHalf
-    const double kPio2Lo = 6.1232339957367660359e-17;
-    const double n = floor(__dadd_rn(__ddiv_rn(x, kPio2Hi), 0.5));
-    const double r = __dsub_rn(__dsub_rn(x, __dmul_rn(n, kPio2Hi)), __dmul_rn(n, kPio2Lo));
-    // For x NaN or infinite, fmod(n, 4) is NaN and r is NaN. The reference
-    // converts that NaN to int (INT_MIN on its x86-64 host) and its switch
-    // takes the default branch, -cos(r): the same branch here keeps even the
-    // NaN's sign bit-identical.
-    const double f = fmod(n, 4.0);
-    int q = (f == f) ? static_cast<int>(f) : 3;
-    if (q < 0) q += 4;
-    switch (q) {
-        case 0: return poly7_sin_reduced(r);
-        case 1: return poly7_cos_reduced(r);
-        case 2: return -poly7_sin_reduced(r);
-        default: return -poly7_cos_reduced(r);
-    }
-}
-
-// kF64Out: the chain result is stored in f64, so sin/cos use CUDA's double
-// routines (about 1 ULP of f64); f32 outputs use the fast reduction +
-// polynomial path above, whose error is far below f32 resolution. With
-// `poly7` Sin is the reference's poly7 family in either case (Cos and the
-// other ops keep the libm family, as resolveFamily does,
-// kernel_buffers.cpp:42-51).
-template <bool kF64Out>
-__device__ __forceinline__ double apply(uint8_t op, double a, double b, bool poly7) {
-    switch (op) {
-        case kAdd: return __dadd_rn(a, b);
-        case kSub: return __dsub_rn(a, b);
-        case kMul: return __dmul_rn(a, b);
-        case kDiv: return b != 0.0 ? __ddiv_rn(a, b) : 0.0;
-        case kNeg: return -a;
-        case kPow: return (a == 2.0 && b == 2.0) ? __dmul_rn(a, a) : ::pow(a, b);
-        case kExp: return ::exp(a);
-        case kLog: return a > 0.0 ? ::log(a) : 0.0;
-        case kSin: return poly7 ? poly7_sin(a) : kF64Out ? ::sin(a) : dev::sin_f64(a);
-        case kCos: {
-            if (kF64Out) return ::cos(a);
-            double s, c;
-            dev::sincos_f64(a, s, c);
-            return c;
-        }
-        case kTan: return ::tan(a);
-        case kTanh: return ::tanh(a);
-        case kSqrt: return a >= 0.0 ? __dsqrt_rn(a) : 0.0;
-        case kRsqrt: return a > 0.0 ? __ddiv_rn(1.0, __dsqrt_rn(a)) : 0.0;
-        case kErf: return ::erf(a);
-        case kGelu: {
-            // 0.5*a*(1 + tanh(c*(a + 0.044715*a*a*a))), left-to-right as in C++.
-            const double a3 = __dmul_rn(__dmul_rn(__dmul_rn(0.044715, a), a), a);
-            const double in = __dmul_rn(0.7978845608028654, __dadd_rn(a, a3));
-            return __dmul_rn(__dmul_rn(0.5, a), __dadd_rn(1.0, ::tanh(in)));
-        }
-        default: return 0.0;
-    }
-}
 
 template <typename T>
 __global__ void chain_kernel(const __grid_constant__ ChainParams p,
@@ -418,11 +323,26 @@ constexpr int kChainTile = kChainThreads * kChainElems;
 constexpr int kChainStages = 4;
 
 // Operand sources: 0 constant, 1 ElemA, 2 ElemB, 3 + s register slot s.
+// `code` is the expression's fused form (below) or -1.
 struct SlotExpr {
     uint8_t op, asrc, bsrc, dst;
-    int32_t pad;
+    int32_t code;
     double aval, bval;
 };
+
+// Fused forms, for the 4-slot instance: an Add, Sub or Mul (op 0..2) whose
+// operand sources (0..6) and destination slot (0..3) are folded into one
+// case label, ((op·7 + asrc)·7 + bsrc)·4 + dst, so the whole expression —
+// both operand reads, the arithmetic over 4 elements and the slot write — is
+// one jump-table dispatch with static register operands, instead of one
+// switch per operand, per operation and per write.
+constexpr int kFusedSrcs = 7;
+constexpr int kFusedSlots = 4;
+constexpr int kFusedOps = 3;
+
+__host__ __device__ constexpr int fusedCode(int op, int asrc, int bsrc, int dst) {
+    return ((op * kFusedSrcs + asrc) * kFusedSrcs + bsrc) * kFusedSlots + dst;
+}
 
 struct SlotChain {
     int32_t n_exprs;
@@ -503,6 +423,60 @@ __device__ __forceinline__ void apply4(uint8_t op, const double (&x)[4], const d
 #undef MLKB_EACH
 }
 
+template <int S, int R>
+__device__ __forceinline__ double fusedSrc(const double (&t)[R][4], const double (&va)[4],
+                                           const double (&vb)[4], double c, int q) {
+    if constexpr (S == 0) return c;
+    else if constexpr (S == 1) return va[q];
+    else if constexpr (S == 2) return vb[q];
+    else return t[S - 3][q];
+}
+
+template <int O, int A, int B, int D, int R>
+__device__ __forceinline__ void fusedStep(double (&t)[R][4], const double (&va)[4],
+                                          const double (&vb)[4], double av, double bv) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const double x = fusedSrc<A, R>(t, va, vb, av, q);
+        const double y = fusedSrc<B, R>(t, va, vb, bv, q);
+        t[D][q] = O == kAdd ? __dadd_rn(x, y) : O == kSub ? __dsub_rn(x, y) : __dmul_rn(x, y);
+    }
+}
+
+// One expression of the 4-slot instance: its fused case when it has one,
+// else the operand / operation / write switches.
+template <bool kF64Out>
+__device__ __forceinline__ void fusedOrGeneric(const SlotExpr& e, double (&t)[4][4],
+                                               const double (&va)[4], const double (&vb)[4],
+                                               bool poly7) {
+#define MLKB_FC(o, a, b, d)                                       \
+    case fusedCode(o, a, b, d):                                   \
+        fusedStep<o, a, b, d, 4>(t, va, vb, e.aval, e.bval);      \
+        break;
+#define MLKB_FC_D(o, a, b) MLKB_FC(o, a, b, 0) MLKB_FC(o, a, b, 1) MLKB_FC(o, a, b, 2) MLKB_FC(o, a, b, 3)
+#define MLKB_FC_B(o, a)                                                                    \
+    MLKB_FC_D(o, a, 0) MLKB_FC_D(o, a, 1) MLKB_FC_D(o, a, 2) MLKB_FC_D(o, a, 3)             \
+    MLKB_FC_D(o, a, 4) MLKB_FC_D(o, a, 5) MLKB_FC_D(o, a, 6)
+#define MLKB_FC_A(o)                                                                       \
+    MLKB_FC_B(o, 0) MLKB_FC_B(o, 1) MLKB_FC_B(o, 2) MLKB_FC_B(o, 3) MLKB_FC_B(o, 4)         \
+    MLKB_FC_B(o, 5) MLKB_FC_B(o, 6)
+    switch (e.code) {
+        MLKB_FC_A(0) MLKB_FC_A(1) MLKB_FC_A(2)
+        default: {
+            double x[4], y[4], r[4];
+            fetch4<4>(e.asrc, e.aval, va, vb, t, x);
+            fetch4<4>(e.bsrc, e.bval, va, vb, t, y);
+            apply4<kF64Out>(e.op, x, y, r, poly7);
+            put4<4>(e.dst, t, r);
+        }
+    }
+#undef MLKB_FC_A
+#undef MLKB_FC_B
+#undef MLKB_FC_D
+#undef MLKB_FC
+}
+static_assert(kAdd == 0 && kSub == 1 && kMul == 2, "fused op numbering");
+
 template <typename T>
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* src, uint32_t bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
@@ -512,7 +486,7 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* src, uint
 }
 
 template <typename T, int R>
-__global__ void __launch_bounds__(kChainThreads)
+__global__ void __launch_bounds__(kChainThreads, 2)
 chain_tile_kernel(const __grid_constant__ SlotChain p, const T* __restrict__ a,
                   const T* __restrict__ b, T* __restrict__ out, int64_t n) {
     extern __shared__ __align__(16) uint8_t chain_smem[];
@@ -570,11 +544,15 @@ chain_tile_kernel(const __grid_constant__ SlotChain p, const T* __restrict__ a,
         double t[R][4];  // every slot is written before it is read (allocateSlots)
         for (int k = 0; k < p.n_exprs; ++k) {
             const SlotExpr& e = p.e[k];
-            double x[4], y[4], r[4];
-            fetch4<R>(e.asrc, e.aval, va, vb, t, x);
-            fetch4<R>(e.bsrc, e.bval, va, vb, t, y);
-            apply4<sizeof(T) == 8>(e.op, x, y, r, p.poly7 != 0);
-            put4<R>(e.dst, t, r);
+            if constexpr (R == kFusedSlots) {
+                fusedOrGeneric<sizeof(T) == 8>(e, t, va, vb, p.poly7 != 0);
+            } else {
+                double x[4], y[4], r[4];
+                fetch4<R>(e.asrc, e.aval, va, vb, t, x);
+                fetch4<R>(e.bsrc, e.bval, va, vb, t, y);
+                apply4<sizeof(T) == 8>(e.op, x, y, r, p.poly7 != 0);
+                put4<R>(e.dst, t, r);
+            }
         }
         double res[4];
         fetch4<R>(static_cast<uint8_t>(3 + p.out_slot), 0.0, va, vb, t, res);
@@ -696,6 +674,12 @@ int allocateSlots(const DevExpr* ex, int n, int limit, SlotChain& sc) {
     sc.n_exprs = n;
     sc.out_slot = slotOf[static_cast<size_t>(n - 1)] >= 0 ? slotOf[static_cast<size_t>(n - 1)]
                                                           : sc.e[n - 1].dst;
+    for (int k = 0; k < n; ++k) {
+        SlotExpr& e = sc.e[k];
+        const bool fusable = used <= kFusedSlots && e.op < kFusedOps && e.asrc < kFusedSrcs &&
+                             e.bsrc < kFusedSrcs && e.dst < kFusedSlots;
+        e.code = fusable ? fusedCode(e.op, e.asrc, e.bsrc, e.dst) : -1;
+    }
     return used;
 }
 
@@ -737,6 +721,43 @@ int checkChain(const mlkb_expr* exprs, int32_t n_exprs, bool has_b) {
     return okStatus();
 }
 
+namespace {
+
+// The device form of a host chain; a ScalarParam operand becomes the
+// constant scalars[idx] (0 past the table's end), as the reference reads it
+// (kernel_buffers.cpp:114-117).
+void fillChainParams(const mlkb_expr* exprs, int32_t n_exprs, int32_t poly7_sin,
+                     const double* scalars, int64_t n_scalars, ChainParams& p) {
+    p.n_exprs = n_exprs;
+    p.poly7 = poly7_sin != 0 ? 1 : 0;
+    for (int k = 0; k < n_exprs; ++k) {
+        const mlkb_expr& x = exprs[k];
+        DevExpr& e = p.e[k];
+        e.op = static_cast<uint8_t>(x.op);
+        e.unary = isUnaryOp(x.op) ? 1 : 0;
+        for (int side = 0; side < 2; ++side) {
+            int kind = side == 0 ? x.a_kind : x.b_kind;
+            const int64_t idx = side == 0 ? x.a_index : x.b_index;
+            double val = side == 0 ? x.a_value : x.b_value;
+            if (kind == kScalar) {  // a ScalarParam is a constant for the whole launch
+                val = (idx >= 0 && idx < n_scalars) ? scalars[idx] : 0.0;
+                kind = kConst;
+            }
+            (side == 0 ? e.akind : e.bkind) = static_cast<uint8_t>(kind);
+            (side == 0 ? e.aidx : e.bidx) = static_cast<int16_t>(kind == kTemp ? idx : 0);
+            (side == 0 ? e.aval : e.bval) = val;
+        }
+    }
+}
+
+void toJit(const ChainParams& p, JitExpr* je) {
+    for (int k = 0; k < p.n_exprs; ++k) {
+        const DevExpr& e = p.e[k];
+        je[k] = JitExpr{e.op, e.akind, e.bkind, e.unary, e.aidx, e.bidx, e.aval, e.bval};
+    }
+}
+
+}  // namespace
 }  // namespace mlkb
 
 extern "C" int mlkb_map_sin_f32(const float* x, float* y, int64_t n, void* stream) {
@@ -764,27 +785,16 @@ extern "C" int mlkb_map_chain(const mlkb_expr* exprs, int32_t n_exprs, int32_t p
         return setError(MLKB_ERR_INVALID, "chain: bad scalar table");
     }
     ChainParams p{};
-    p.n_exprs = n_exprs;
-    p.poly7 = poly7_sin != 0 ? 1 : 0;
-    for (int k = 0; k < n_exprs; ++k) {
-        const mlkb_expr& x = exprs[k];
-        DevExpr& e = p.e[k];
-        e.op = static_cast<uint8_t>(x.op);
-        e.unary = isUnaryOp(x.op) ? 1 : 0;
-        for (int side = 0; side < 2; ++side) {
-            int kind = side == 0 ? x.a_kind : x.b_kind;
-            const int64_t idx = side == 0 ? x.a_index : x.b_index;
-            double val = side == 0 ? x.a_value : x.b_value;
-            if (kind == kScalar) {  // a ScalarParam is a constant for the whole launch
-                val = (idx >= 0 && idx < n_scalars) ? scalars[idx] : 0.0;
-                kind = kConst;
-            }
-            (side == 0 ? e.akind : e.bkind) = static_cast<uint8_t>(kind);
-            (side == 0 ? e.aidx : e.bidx) = static_cast<int16_t>(kind == kTemp ? idx : 0);
-            (side == 0 ? e.aval : e.bval) = val;
-        }
-    }
+    fillChainParams(exprs, n_exprs, poly7_sin, scalars, n_scalars, p);
     cudaStream_t s = asStream(stream);
+    // A compiled straight-line kernel for the chain when run-time
+    // compilation is available (chain_jit.cpp), else an interpreter.
+    {
+        JitExpr je[kMaxExprs];
+        toJit(p, je);
+        const int st = launchChainJit(je, n_exprs, p.poly7 != 0, a, b, out, elem_dtype, n, s);
+        if (st != kJitUnavailable) return st;
+    }
     // The register-slot interpreter when the chain fits 8 slots and every
     // buffer is 16-byte aligned (cp.async and vector stores); else the
     // local-array interpreter below.
@@ -821,4 +831,22 @@ extern "C" int mlkb_map_chain(const mlkb_expr* exprs, int32_t n_exprs, int32_t p
                                                   static_cast<double*>(out), n);
     }
     return checkLaunch("chain kernel launch");
+}
+
+extern "C" int mlkb_chain_build(const mlkb_expr* exprs, int32_t n_exprs, int32_t poly7_sin,
+                                int32_t elem_dtype, int32_t has_b) {
+    using namespace mlkb;
+    if (int st = checkChain(exprs, n_exprs, has_b != 0)) return st;
+    if (elem_dtype != MLKB_F32 && elem_dtype != MLKB_F64) {
+        return setError(MLKB_ERR_INVALID, "chain: element dtype must be f32 or f64");
+    }
+    ChainParams p{};
+    fillChainParams(exprs, n_exprs, poly7_sin, nullptr, 0, p);
+    JitExpr je[kMaxExprs];
+    toJit(p, je);
+    const char* why = nullptr;
+    if (buildChainJit(je, n_exprs, p.poly7 != 0, elem_dtype, &why) == kJitUnavailable) {
+        return setError(MLKB_ERR_UNSUPPORTED, why != nullptr ? why : "chain compilation unavailable");
+    }
+    return okStatus();
 }

@@ -1,0 +1,80 @@
+"""Run-time chain compilation on the host (NVRTC compiles to an sm_100a cubin
+without a GPU): every op and operand form the golden chains use compiles, the
+mode switch works, bad chains are refused before any compilation, and a chain
+structure compiles once whatever its constant values."""
+import numpy as np
+import pytest
+
+import mlk2_b200 as mb
+from mlk2_b200 import api, kir
+
+A, B, C, S, T, E = kir.A, kir.B, kir.C, kir.S, kir.T, kir.E
+
+
+def _nvrtc_or_skip():
+    prev = api.chain_compile(-1)[0]
+    api.chain_compile(1)
+    active = api.chain_compile(-1)[0]
+    if not prev:
+        api.chain_compile(0)
+    if not active:
+        pytest.skip("NVRTC is not loadable on this host")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f64"])
+@pytest.mark.parametrize("poly7", [False, True])
+def test_every_golden_chain_compiles(golden, dtype, poly7):
+    _nvrtc_or_skip()
+    g = golden("chains")
+    for name in [k[2:] for k in g.files if k.startswith("c_")]:
+        ch = g["c_" + name]
+        uses_b = any(int(e["a_kind"]) == 2 or int(e["b_kind"]) == 2 for e in ch)
+        api.chain_build(ch, dtype=dtype, has_b=uses_b, poly7=poly7)
+
+
+def test_every_op_in_one_chain_compiles():
+    _nvrtc_or_skip()
+    unary = ("neg", "exp", "log", "sin", "cos", "tan", "tanh", "sqrt", "rsqrt", "erf", "gelu")
+    ex = [E("mul", A, C(0.125))]
+    for op in ("add", "sub", "mul", "div", "pow") + unary:
+        ex.append(E(op, T(len(ex) - 1)) if op in unary else E(op, T(len(ex) - 1), B))
+    api.chain_build(kir.chain(*ex), dtype="f32", has_b=True)
+    # the longest chain the ABI admits (64 expressions)
+    long = [E("mul", A, C(1.0))] + [E("add", T(k), C(k)) for k in range(63)]
+    api.chain_build(kir.chain(*long), dtype="f64")
+
+
+def test_structure_compiles_once_whatever_the_constants():
+    _nvrtc_or_skip()
+    _, before, _ = api.chain_compile(-1)
+    for v in (1.0, 2.0, -3.5, 1e300):
+        api.chain_build(kir.chain(E("mul", A, C(v)), E("sub", T(0), S(3)), E("exp", T(1))),
+                        dtype="f32")
+    _, after, _ = api.chain_compile(-1)
+    assert after - before <= 1
+
+
+def test_mode_switch():
+    _nvrtc_or_skip()
+    try:
+        assert api.chain_compile(0)[0] is False
+        assert api.chain_compile(-1)[0] is False       # a query changes nothing
+        assert api.chain_compile(7)[0] is False        # neither does an unknown mode
+        assert api.chain_compile(1)[0] is True
+    finally:
+        api.chain_compile(1)
+
+
+def test_bad_chains_refused_before_compiling():
+    _, before, _ = api.chain_compile(-1)
+    bad_op = kir.chain(E("mul", A, A))
+    bad_op["op"][0] = 99
+    with pytest.raises(mb.MLKBError):
+        api.chain_build(bad_op)
+    forward_temp = kir.chain(E("add", T(1), A), E("mul", A, A))
+    with pytest.raises(mb.MLKBError):
+        api.chain_build(forward_temp)
+    with pytest.raises(mb.MLKBError):                  # ElemB without a b buffer
+        api.chain_build(kir.chain(E("mul", A, B)), has_b=False)
+    _, after, _ = api.chain_compile(-1)
+    assert after == before

@@ -133,7 +133,7 @@ ARITH = {"add", "sub", "mul", "div", "neg", "pow22", "scalar", "poly", "sqrt", "
 
 
 @pytest.mark.parametrize("dtype", ["f32", "f64"])
-def test_generic_chain_every_op(cuda, golden, dtype):
+def test_generic_chain_every_op(cuda, golden, dtype, chain_path):
     g = golden("chains")
     npdt = np.float32 if dtype == "f32" else np.float64
     xa = dev(cuda, g["xa"].astype(npdt))

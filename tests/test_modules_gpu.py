@@ -32,7 +32,7 @@ def same_bits(a, b):
     return True
 
 
-def test_poly7_bit_exact(cuda, golden):
+def test_poly7_bit_exact(cuda, golden, chain_path):
     g = golden("map_poly7")
     # f64 inputs, f64 outputs: bit for bit (NaN as a class)
     x = dev(cuda, g["x"])
@@ -106,7 +106,7 @@ def test_pipeline_modules_reference_abi(cuda, golden):
         assert oracle.ulp_f64(out, np.array([want])).max() <= 4
 
 
-def test_scalar_table_of_any_size(cuda):
+def test_scalar_table_of_any_size(cuda, chain_path):
     # ScalarParam 100 of a 150-entry table, and 200 past its end (reads 0)
     ch = kir.chain(kir.E("mul", kir.A, kir.S(100)), kir.E("add", kir.T(0), kir.S(5)),
                    kir.E("add", kir.T(1), kir.S(200)))
@@ -157,7 +157,7 @@ def _wide_chain(live):
 
 @pytest.mark.parametrize("dtype", [np.float32, np.float64])
 @pytest.mark.parametrize("live", [2, 6, 11])
-def test_chain_slot_allocation_paths(cuda, dtype, live):
+def test_chain_slot_allocation_paths(cuda, dtype, live, chain_path):
     # 2 live temps: 4 register slots; 6: 8 slots; 11: the local-array
     # interpreter. Arithmetic chains are bit-exact in f64 and round once to
     # f32, so both dtypes must equal the oracle exactly.
@@ -172,7 +172,7 @@ def test_chain_slot_allocation_paths(cuda, dtype, live):
         assert np.array_equal(got, want[off:].astype(dtype).astype(np.float64)), (live, off)
 
 
-def test_chain_two_inputs_and_tail(cuda):
+def test_chain_two_inputs_and_tail(cuda, chain_path):
     # ElemA and ElemB through the staged loads, lengths around a tile edge
     ch = kir.chain(kir.E("mul", kir.A, kir.B), kir.E("div", kir.T(0), kir.B),
                    kir.E("add", kir.T(1), kir.A))
@@ -185,3 +185,20 @@ def test_chain_two_inputs_and_tail(cuda):
         api.map_chain(ch, dev(cuda, ah), y, b=dev(cuda, bh))
         (want,) = oracle.port().chain([ch], ah, bh)
         assert np.array_equal(host(y), want), n
+
+
+def test_compiled_chain_reused_across_constants_and_scalars(cuda):
+    # one compiled kernel per chain structure: other constant or scalar values
+    # reuse it, and each call still computes with its own values
+    api.chain_compile(1)
+    xh = np.linspace(-4, 4, 4099)
+    x = dev(cuda, xh)
+    _, c0, _ = api.chain_compile(-1)
+    for v in (0.5, 3.0, -1.25):
+        ch = kir.chain(kir.E("mul", kir.A, kir.C(v)), kir.E("add", kir.T(0), kir.S(1)))
+        y = empty(cuda, x.shape, cuda.float64)
+        api.map_chain(ch, x, y, scalars=[0.0, 2 * v])
+        (want,) = oracle.port().chain([ch], xh, scalars=[0.0, 2 * v])
+        assert same_bits(host(y), want), v
+    _, c1, _ = api.chain_compile(-1)
+    assert c1 - c0 <= 1, (c0, c1)

@@ -351,7 +351,7 @@ def main():
                     help="headline warm-up continues at least this long (clock samples); "
                          "also the run-in of each config's sustained figure (0: none)")
     ap.add_argument("--case", default=None,
-                    choices=["map1", "map2", "softmax", "gemm", "gemm_f32", "qk", "qk_kt"],
+                    choices=["map1", "map2", "chain", "softmax", "gemm", "gemm_f32", "qk", "qk_kt"],
                     help="run one kernel W+K times (profiling target), no JSON line")
     ap.add_argument("--detail", default=None,
                     help="also write the full (verbose) record as JSON to this path")
@@ -653,6 +653,18 @@ def run_case(args):
         api.fill(x, SEED, 2, "uniform", -8.0, 8.0)
         y, dy = torch.empty_like(x), torch.empty_like(x)
         fn = (lambda: api.map_sin_dsin(x, y, dy)) if c == "map2" else (lambda: api.map_sin(x, y))
+    elif c == "chain":  # the pipeline's derivative chain through the compiled chain path
+        import numpy as np
+
+        from mlk2_b200 import kir
+
+        pipe = np.load(os.path.join(ROOT, "tests", "golden", "pipeline.npz"))
+        dchain = kir.chains_of(json.loads(str(pipe["dsin_json"])))[-1]
+        n = sz or (1 << 26)
+        x = torch.empty(n, device="cuda")
+        api.fill(x, SEED, 7, "uniform", -8.0, 8.0)
+        y = torch.empty_like(x)
+        fn = lambda: api.map_chain(dchain, x, y)  # noqa: E731
     elif c == "softmax":
         rows = sz or 16384
         x = torch.empty((rows, 4096), device="cuda")

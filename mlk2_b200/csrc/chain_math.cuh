@@ -64,15 +64,43 @@ __device__ __forceinline__ void sincos_f64(double u, double& s, double& c) {
     }
 }
 
+// sin_poly(r, z) when `cosine` is false, cos_poly(z) when it is true, as one
+// Horner chain whose coefficients are selected per element, so a warp whose
+// lanes need different polynomials runs one chain instead of both. The
+// result is bit-identical to calling the chosen function: the sine chain is
+// given a leading zero coefficient, and fma(z, 0, s) = s exactly for the
+// finite z = r*r of a reduced argument.
+__device__ __forceinline__ double sin_or_cos_poly(double r, double z, bool cosine) {
+    double p = cosine ? 2.08767569878681e-09 : 0.0;
+    p = fma(z, p, cosine ? -2.755731922398589e-07 : -2.505210838544172e-08);
+    p = fma(z, p, cosine ? 2.48015873015873e-05 : 2.7557319223985893e-06);
+    p = fma(z, p, cosine ? -1.388888888888889e-03 : -1.984126984126984e-04);
+    p = fma(z, p, cosine ? 4.1666666666666664e-02 : 8.333333333333333e-03);
+    p = fma(z, p, cosine ? -0.5 : -1.6666666666666666e-01);
+    return fma(cosine ? z : r * z, p, cosine ? 1.0 : r);
+}
+
 __device__ __forceinline__ double sin_f64(double u) {
     if (fabs(u) < 1048576.0) {
         int q;
         const double r = reduce_pio2(u, q);
-        const double z = r * r;
-        const double v = (q & 1) ? cos_poly(z) : sin_poly(r, z);
+        const double v = sin_or_cos_poly(r, r * r, (q & 1) != 0);
         return (q & 2) ? -v : v;
     }
     return ::sin(u);
+}
+
+// cos(u) alone: the same value as sincos_f64's c, with one polynomial.
+__device__ __forceinline__ double cos_f64(double u) {
+    if (fabs(u) < 1048576.0) {
+        int q;
+        const double r = reduce_pio2(u, q);
+        const double v = sin_or_cos_poly(r, r * r, (q & 1) == 0);
+        return ((q + 1) & 2) ? -v : v;
+    }
+    double s, c;
+    ::sincos(u, &s, &c);
+    return c;
 }
 
 // exp(d) in f64 for d <= 0 (softmax exponents). Values below -120 return 0:
@@ -186,12 +214,7 @@ __device__ __forceinline__ double apply(unsigned op, double a, double b, bool po
         case kExp: return ::exp(a);
         case kLog: return a > 0.0 ? ::log(a) : 0.0;
         case kSin: return poly7 ? poly7_sin(a) : kF64Out ? ::sin(a) : dev::sin_f64(a);
-        case kCos: {
-            if (kF64Out) return ::cos(a);
-            double s, c;
-            dev::sincos_f64(a, s, c);
-            return c;
-        }
+        case kCos: return kF64Out ? ::cos(a) : dev::cos_f64(a);
         case kTan: return ::tan(a);
         case kTanh: return ::tanh(a);
         case kSqrt: return a >= 0.0 ? __dsqrt_rn(a) : 0.0;

@@ -192,10 +192,14 @@ int mlkb_module_run_dev(const mlkb_module* module, void* const* bufs,
  * copies outputs back, synchronously. n_gpus == 1 runs on the calling
  * thread's current device; n_gpus > 1 splits the work into contiguous
  * element / row shards over devices 0..n_gpus-1 (n_gpus <= 0: all visible
- * devices), one host thread and stream per device. Copies go straight
- * between the caller's buffers and the device: page-locked host buffers
- * copy at full PCIe speed and overlap with compute, pageable ones are
- * copied by the CUDA driver's own staging, without that overlap.
+ * devices), one host thread and stream per device. Page-locked (pinned)
+ * host buffers are copied straight to and from the device, overlapped with
+ * compute. Pageable buffers (ordinary malloc / std::vector memory, as the
+ * reference's LoadedKernel::run passes) are staged by the library: a
+ * multi-threaded CPU copy into pinned buffers it keeps per device (grow-only,
+ * about 16 MB per buffer and pipeline step for maps, 64 MB for whole-buffer
+ * kinds), then the DMA; for maps the CPU copies of one step overlap the
+ * device work of the next. The same staging serves mlk_kernel.
  * Kinds: fused maps (element shards), Softmax / ReduceSum / MatMul (row
  * shards, MatMul's B on every device) and the scaled-scores composite (row
  * shards of Q, S, Sc and Y, Kt on every device). A module with nothing to

@@ -107,30 +107,38 @@ int jitMode() {
 }
 
 // ---- source generation -----------------------------------------------------------
-// The kernel around the chain: a grid-stride loop over 16-byte vectors
-// (kUnroll of them in flight per thread, streaming loads and stores) when
-// every buffer is 16-byte aligned, then an element loop for the tail or for
-// unaligned buffers. Launched with programmatic stream serialization, like
-// the other map kernels: it waits for the preceding grid before touching
-// memory and lets the next grid's blocks be scheduled as its own retire.
-const char kKernelSrc[] = R"MLKB(
+// One kernel evaluates a GROUP of chains (the roots of a map module that read
+// the same inputs over the same range; a lone chain is a group of one): the
+// inputs are loaded once and every chain's result is stored to its own
+// output. The loop: a grid-stride loop over 16-byte vectors (kJitUnroll of
+// them in flight per thread, streaming loads and stores) when every buffer is
+// 16-byte aligned, then an element loop for the tail or for unaligned
+// buffers. Launched with programmatic stream serialization, like the other
+// map kernels: it waits for the preceding grid before touching memory and
+// lets the next grid's blocks be scheduled as its own retire.
+const char kPreludeSrc[] = R"MLKB(
 template <typename V> struct MlkbVec;
 template <> struct MlkbVec<float> { typedef float4 V; enum { kN = 4 }; };
 template <> struct MlkbVec<double> { typedef double2 V; enum { kN = 2 }; };
-
+struct MlkbOuts { MlkbT* p[8]; };
+template <int R> __device__ double mlkb_eval(double A, double B, const MlkbConsts& c);
+template <int R>
 __device__ __forceinline__ float4 mlkb_eval_vec(float4 x, float4 y, const MlkbConsts& c) {
-    return make_float4(static_cast<float>(mlkb_eval(x.x, y.x, c)),
-                       static_cast<float>(mlkb_eval(x.y, y.y, c)),
-                       static_cast<float>(mlkb_eval(x.z, y.z, c)),
-                       static_cast<float>(mlkb_eval(x.w, y.w, c)));
+    return make_float4(static_cast<float>(mlkb_eval<R>(x.x, y.x, c)),
+                       static_cast<float>(mlkb_eval<R>(x.y, y.y, c)),
+                       static_cast<float>(mlkb_eval<R>(x.z, y.z, c)),
+                       static_cast<float>(mlkb_eval<R>(x.w, y.w, c)));
 }
+template <int R>
 __device__ __forceinline__ double2 mlkb_eval_vec(double2 x, double2 y, const MlkbConsts& c) {
-    return make_double2(mlkb_eval(x.x, y.x, c), mlkb_eval(x.y, y.y, c));
+    return make_double2(mlkb_eval<R>(x.x, y.x, c), mlkb_eval<R>(x.y, y.y, c));
 }
+)MLKB";
 
+const char kKernelHead[] = R"MLKB(
 extern "C" __global__ void __launch_bounds__(256)
 mlkb_chain_kernel(const MlkbT* __restrict__ a, const MlkbT* __restrict__ b,
-                  MlkbT* __restrict__ out, long long n, int vec,
+                  const __grid_constant__ MlkbOuts o, long long n, int vec,
                   const __grid_constant__ MlkbConsts c) {
     typedef typename MlkbVec<MlkbT>::V V;
     const int kN = MlkbVec<MlkbT>::kN;
@@ -143,7 +151,6 @@ mlkb_chain_kernel(const MlkbT* __restrict__ a, const MlkbT* __restrict__ b,
         const long long nv = n / kN;
         const V* av = reinterpret_cast<const V*>(a);
         const V* bv = reinterpret_cast<const V*>(b);
-        V* ov = reinterpret_cast<V*>(out);
         for (long long base = tid; base < nv; base += nth * MLKB_UNROLL) {
             V x[MLKB_UNROLL] = {}, y[MLKB_UNROLL] = {};
 #pragma unroll
@@ -157,7 +164,11 @@ mlkb_chain_kernel(const MlkbT* __restrict__ a, const MlkbT* __restrict__ b,
 #pragma unroll
             for (int u = 0; u < MLKB_UNROLL; ++u) {
                 const long long i = base + u * nth;
-                if (i < nv) __stcs(ov + i, mlkb_eval_vec(x[u], y[u], c));
+                if (i < nv) {
+)MLKB";
+
+const char kKernelMid[] = R"MLKB(
+                }
             }
         }
         done = nv * kN;
@@ -165,23 +176,26 @@ mlkb_chain_kernel(const MlkbT* __restrict__ a, const MlkbT* __restrict__ b,
     for (long long i = done + tid; i < n; i += nth) {
         const double va = MLKB_USES_A ? static_cast<double>(a[i]) : 0.0;
         const double vb = MLKB_USES_B ? static_cast<double>(b[i]) : 0.0;
-        out[i] = static_cast<MlkbT>(mlkb_eval(va, vb, c));
+)MLKB";
+
+const char kKernelTail[] = R"MLKB(
     }
 }
 )MLKB";
 
-// A chain's generated source. The text determines the compiled kernel, so it
-// is also the cache key; constants are numbered in operand order and read
-// from the kernel's parameter block.
+// A group's generated source. The text determines the compiled kernel, so it
+// is also the cache key; constants are numbered in operand order over all
+// chains and read from the kernel's parameter block.
 struct Generated {
     std::string src;
     std::vector<double> consts;
     bool usesA = false, usesB = false;
 };
 
-Generated generate(const JitExpr* e, int n, bool poly7, bool f64) {
+Generated generate(const JitExpr* const* chains, const int* ns, const bool* poly7, int nChains,
+                   bool f64) {
     Generated g;
-    std::string body;
+    std::string evals;
     char buf[256];
     auto operand = [&](int kind, int idx, double val) -> std::string {
         switch (kind) {
@@ -196,16 +210,25 @@ Generated generate(const JitExpr* e, int n, bool poly7, bool f64) {
                 return buf;
         }
     };
-    for (int k = 0; k < n; ++k) {
-        const std::string x = operand(e[k].akind, e[k].aidx, e[k].aval);
-        const std::string y = e[k].unary ? std::string("0.0") : operand(e[k].bkind, e[k].bidx, e[k].bval);
-        std::snprintf(buf, sizeof buf, "    const double t%d = mlkb::chain::apply<%s>(%uu, ", k,
-                      f64 ? "true" : "false", static_cast<unsigned>(e[k].op));
-        body += buf;
-        body += x + ", " + y + (poly7 ? ", true);\n" : ", false);\n");
+    for (int j = 0; j < nChains; ++j) {
+        const JitExpr* e = chains[j];
+        std::snprintf(buf, sizeof buf,
+                      "template <> __device__ __forceinline__ double mlkb_eval<%d>("
+                      "double A, double B, const MlkbConsts& c) {\n"
+                      "    (void)A; (void)B; (void)c;\n", j);
+        evals += buf;
+        for (int k = 0; k < ns[j]; ++k) {
+            const std::string x = operand(e[k].akind, e[k].aidx, e[k].aval);
+            const std::string y =
+                e[k].unary ? std::string("0.0") : operand(e[k].bkind, e[k].bidx, e[k].bval);
+            std::snprintf(buf, sizeof buf, "    const double t%d = mlkb::chain::apply<%s>(%uu, ",
+                          k, f64 ? "true" : "false", static_cast<unsigned>(e[k].op));
+            evals += buf;
+            evals += x + ", " + y + (poly7[j] ? ", true);\n" : ", false);\n");
+        }
+        std::snprintf(buf, sizeof buf, "    return t%d;\n}\n", ns[j] - 1);
+        evals += buf;
     }
-    std::snprintf(buf, sizeof buf, "    return t%d;\n", n - 1);
-    body += buf;
     const size_t nc = g.consts.empty() ? 1 : g.consts.size();
     std::snprintf(buf, sizeof buf,
                   "#include \"mlkb_chain_math.cuh\"\n"
@@ -214,10 +237,22 @@ Generated generate(const JitExpr* e, int n, bool poly7, bool f64) {
                   "struct MlkbConsts { double v[%zu]; };\n",
                   f64 ? "double" : "float", kJitUnroll, g.usesA ? 1 : 0, g.usesB ? 1 : 0, nc);
     g.src = buf;
-    g.src += "__device__ __forceinline__ double mlkb_eval(double A, double B, const MlkbConsts& c) {\n";
-    g.src += "    (void)A; (void)B; (void)c;\n";
-    g.src += body + "}\n";
-    g.src += kKernelSrc;
+    g.src += kPreludeSrc;
+    g.src += evals;
+    g.src += kKernelHead;
+    for (int j = 0; j < nChains; ++j) {  // vector stores, one per chain
+        std::snprintf(buf, sizeof buf,
+                      "                    __stcs(reinterpret_cast<V*>(o.p[%d]) + i, "
+                      "mlkb_eval_vec<%d>(x[u], y[u], c));\n", j, j);
+        g.src += buf;
+    }
+    g.src += kKernelMid;
+    for (int j = 0; j < nChains; ++j) {  // element stores
+        std::snprintf(buf, sizeof buf,
+                      "        o.p[%d][i] = static_cast<MlkbT>(mlkb_eval<%d>(va, vb, c));\n", j, j);
+        g.src += buf;
+    }
+    g.src += kKernelTail;
     return g;
 }
 
@@ -279,11 +314,14 @@ Compiled* entryFor(const std::string& src) {
 
 }  // namespace
 
-int launchChainJit(const JitExpr* e, int n_exprs, bool poly7, const void* a, const void* b,
-                   void* out, int dtype, int64_t n, cudaStream_t s) {
-    if (jitMode() == 0 || !nvrtc().ok) return kJitUnavailable;
+int launchChainsJit(const JitExpr* const* chains, const int* n_exprs, const bool* poly7,
+                    int n_chains, const void* a, const void* b, void* const* outs, int dtype,
+                    int64_t n, cudaStream_t s) {
+    if (jitMode() == 0 || !nvrtc().ok || n_chains < 1 || n_chains > kMaxJitOuts) {
+        return kJitUnavailable;
+    }
     const bool f64 = dtype == MLKB_F64;
-    Generated g = generate(e, n_exprs, poly7, f64);
+    Generated g = generate(chains, n_exprs, poly7, n_chains, f64);
     if ((g.usesA && a == nullptr) || (g.usesB && b == nullptr)) return kJitUnavailable;
     Compiled* c = entryFor(g.src);
     if (!c->error.empty()) return kJitUnavailable;
@@ -315,7 +353,14 @@ int launchChainJit(const JitExpr* e, int n_exprs, bool poly7, const void* a, con
             if (dev >= 0 && dev < 64) c->blocksPerSm[dev] = per;
         }
     }
-    const bool vec = aligned16(a) && aligned16(b) && aligned16(out);
+    struct {
+        void* p[8];
+    } o = {};
+    bool vec = aligned16(a) && aligned16(b);
+    for (int j = 0; j < n_chains; ++j) {
+        o.p[j] = outs[j];
+        vec = vec && aligned16(outs[j]);
+    }
     // threads wanted: one per kJitUnroll vectors (16 B each), or one per element
     const int64_t units = vec ? (n / (f64 ? 2 : 4) + kJitUnroll - 1) / kJitUnroll : n;
     const int64_t need = (units + kJitThreads - 1) / kJitThreads;
@@ -326,7 +371,7 @@ int launchChainJit(const JitExpr* e, int n_exprs, bool poly7, const void* a, con
     if (consts.empty()) consts.push_back(0.0);
     long long nn = n;
     int vflag = vec ? 1 : 0;
-    void* args[6] = {const_cast<void**>(&a), const_cast<void**>(&b), &out, &nn, &vflag,
+    void* args[6] = {const_cast<void**>(&a), const_cast<void**>(&b), &o, &nn, &vflag,
                      consts.data()};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -344,12 +389,24 @@ int launchChainJit(const JitExpr* e, int n_exprs, bool poly7, const void* a, con
     return okStatus();
 }
 
+int launchChainJit(const JitExpr* e, int n_exprs, bool poly7, const void* a, const void* b,
+                   void* out, int dtype, int64_t n, cudaStream_t s) {
+    const JitExpr* chains[1] = {e};
+    const int ns[1] = {n_exprs};
+    const bool p7[1] = {poly7};
+    void* outs[1] = {out};
+    return launchChainsJit(chains, ns, p7, 1, a, b, outs, dtype, n, s);
+}
+
 int buildChainJit(const JitExpr* e, int n_exprs, bool poly7, int dtype, const char** why) {
     if (!nvrtc().ok) {
         if (why) *why = nvrtc().why.c_str();
         return kJitUnavailable;
     }
-    Generated g = generate(e, n_exprs, poly7, dtype == MLKB_F64);
+    const JitExpr* chains[1] = {e};
+    const int ns[1] = {n_exprs};
+    const bool p7[1] = {poly7};
+    Generated g = generate(chains, ns, p7, 1, dtype == MLKB_F64);
     const Compiled* c = entryFor(g.src);  // entries live as long as the process
     if (!c->error.empty()) {
         if (why) *why = c->error.c_str();

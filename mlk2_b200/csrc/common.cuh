@@ -42,6 +42,17 @@ constexpr int kJitUnavailable = -100;
 // MLKB_F64) as a compiled straight-line kernel, compiling it on first use.
 int launchChainJit(const JitExpr* e, int n_exprs, bool poly7, const void* a, const void* b,
                    void* out, int dtype, int64_t n, cudaStream_t s);
+// The same for a GROUP of at most kMaxJitOuts chains that read the same a
+// (and b) over the same n elements: one kernel loads the inputs once and
+// stores chain j's result to outs[j]. poly7[j] selects chain j's Sin family.
+constexpr int kMaxJitOuts = 8;
+int launchChainsJit(const JitExpr* const* chains, const int* n_exprs, const bool* poly7,
+                    int n_chains, const void* a, const void* b, void* const* outs, int dtype,
+                    int64_t n, cudaStream_t s);
+// A host chain in the compiled form: checked as mlkb_map_chain checks it
+// (MLKB_OK or an error status), ScalarParams resolved against the table.
+int toJitChain(const mlkb_expr* exprs, int32_t n_exprs, bool has_b, const double* scalars,
+               int64_t n_scalars, JitExpr* out);
 // Compiles (and caches) the chain's kernel without launching it; *why gets
 // the reason when it returns kJitUnavailable.
 int buildChainJit(const JitExpr* e, int n_exprs, bool poly7, int dtype, const char** why);

@@ -760,6 +760,20 @@ void toJit(const ChainParams& p, JitExpr* je) {
 }  // namespace
 }  // namespace mlkb
 
+namespace mlkb {
+int toJitChain(const mlkb_expr* exprs, int32_t n_exprs, bool has_b, const double* scalars,
+               int64_t n_scalars, JitExpr* out) {
+    if (int st = checkChain(exprs, n_exprs, has_b)) return st;
+    if (n_scalars < 0 || (n_scalars > 0 && scalars == nullptr)) {
+        return setError(MLKB_ERR_INVALID, "chain: bad scalar table");
+    }
+    ChainParams p{};
+    fillChainParams(exprs, n_exprs, 0, scalars, n_scalars, p);
+    toJit(p, out);
+    return okStatus();
+}
+}  // namespace mlkb
+
 extern "C" int mlkb_map_sin_f32(const float* x, float* y, int64_t n, void* stream) {
     return mlkb::launchMap<mlkb::SinOp>(x, y, nullptr, n, stream);
 }

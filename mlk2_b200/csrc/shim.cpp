@@ -518,14 +518,65 @@ char* offsetPtr(void* p, int64_t elems, int dtype) {
 
 // Which kernel runs each root of a map module (in root order):
 // kMapSin / kMapSinDsin (the dedicated f32 kernels, the latter also taking
-// root `q`, a derivative root over the same input and range) or kMapChain
-// (the generic chain interpreter).
-enum MapKernel { kMapSin = 1, kMapSinDsin = 2, kMapChain = 3 };
+// root `q`, a derivative root over the same input and range), kMapChain (the
+// generic chain path) or kMapChains (the generic chain path for a group of
+// roots in one kernel: roots r and group[1..]).
+enum MapKernel { kMapSin = 1, kMapSinDsin = 2, kMapChain = 3, kMapChains = 4 };
 
 struct MapLaunch {
     MapKernel kernel;
     size_t r, q;
+    std::vector<size_t> group;  // kMapChains: the roots, in order
 };
+
+// Consecutive generic-chain launches whose roots read the same inputs over
+// the same range become one kMapChains launch: every root of the group reads
+// only those inputs (the Compute chain's ElemA / ElemB), no root of the group
+// writes one of them, and the outputs are distinct buffers, so evaluating the
+// roots element by element in one kernel gives what the executor's root-by-
+// root order gives (kernel_buffers.cpp:921-953). At most kMaxJitOuts roots.
+void groupChains(const Module& m, std::vector<MapLaunch>& plan) {
+    std::vector<MapLaunch> out;
+    for (size_t i = 0; i < plan.size(); ++i) {
+        if (plan[i].kernel != kMapChain) {
+            out.push_back(plan[i]);
+            continue;
+        }
+        const MapRoot& first = m.roots[plan[i].r];
+        std::vector<size_t> group{plan[i].r};
+        int groupB = first.b;  // the second input, shared by the roots that read one
+        size_t j = i + 1;
+        for (; j < plan.size() && group.size() < static_cast<size_t>(kMaxJitOuts); ++j) {
+            if (plan[j].kernel != kMapChain) break;
+            const MapRoot& o = m.roots[plan[j].r];
+            if (o.a != first.a || (o.b >= 0 && groupB >= 0 && o.b != groupB) ||
+                o.begin != first.begin || o.end != first.end) {
+                break;
+            }
+            if (o.b >= 0) groupB = o.b;
+            bool ok = true;
+            for (size_t g : group) {
+                const MapRoot& x = m.roots[g];
+                ok = ok && x.out != o.out;
+            }
+            if (!ok) break;
+            group.push_back(plan[j].r);
+        }
+        bool inputsSafe = true;  // no output of the group is one of its inputs
+        for (size_t g : group) {
+            const MapRoot& x = m.roots[g];
+            inputsSafe = inputsSafe && x.out != first.a && (groupB < 0 || x.out != groupB);
+        }
+        if (group.size() > 1 && inputsSafe) {
+            MapLaunch l{kMapChains, group[0], group[0], group};
+            out.push_back(l);
+            i = j - 1;
+        } else {
+            out.push_back(plan[i]);
+        }
+    }
+    plan.swap(out);
+}
 
 std::vector<MapLaunch> planMap(const Module& m, const int32_t* dt) {
     std::vector<MapLaunch> plan;
@@ -564,7 +615,52 @@ std::vector<MapLaunch> planMap(const Module& m, const int32_t* dt) {
             plan.push_back({kMapSin, r, r});
         }
     }
+    groupChains(m, plan);
     return plan;
+}
+
+// One kMapChains launch: the group's chains compiled into one kernel, or,
+// where chains are not compiled, each root on its own as kMapChain runs it.
+int runChainGroup(const Module& m, const MapLaunch& l, void* const* bufs, const int32_t* dt,
+                  void* a, void* b, int64_t cnt, const double* scalars, int64_t n_scalars,
+                  void* stream) {
+    const MapRoot& first = m.roots[l.r];
+    const int dtOut = dtypeAt(dt, m, first.out);
+    const size_t g = l.group.size();
+    for (size_t j : l.group) {  // the group's second input, if a root reads one
+        if (b == nullptr && m.roots[j].b >= 0) {
+            b = offsetPtr(bufAt(bufs, m, m.roots[j].b), first.begin, dtOut);
+        }
+    }
+    std::vector<std::vector<JitExpr>> chains(g);
+    std::vector<const JitExpr*> cp(g);
+    std::vector<int> ns(g);
+    std::vector<void*> outs(g);
+    bool p7[kMaxJitOuts] = {};
+    for (size_t j = 0; j < g; ++j) {
+        const MapRoot& r = m.roots[l.group[j]];
+        chains[j].resize(r.chain.size());
+        if (int st = toJitChain(r.chain.data(), static_cast<int32_t>(r.chain.size()), b != nullptr,
+                                scalars, n_scalars, chains[j].data())) {
+            return st;
+        }
+        cp[j] = chains[j].data();
+        ns[j] = static_cast<int>(r.chain.size());
+        outs[j] = offsetPtr(bufAt(bufs, m, r.out), r.begin, dtOut);
+        p7[j] = r.poly7;
+    }
+    const int st = launchChainsJit(cp.data(), ns.data(), p7, static_cast<int>(g), a, b,
+                                   outs.data(), dtOut, cnt, asStream(stream));
+    if (st != kJitUnavailable) return st;
+    for (size_t j = 0; j < g; ++j) {
+        const MapRoot& r = m.roots[l.group[j]];
+        if (int s2 = mlkb_map_chain(r.chain.data(), static_cast<int32_t>(r.chain.size()),
+                                    r.poly7 ? 1 : 0, a, b, outs[j], dtOut, cnt, scalars,
+                                    n_scalars, stream)) {
+            return s2;
+        }
+    }
+    return okStatus();
 }
 
 int runMapDev(const Module& m, void* const* bufs, const int32_t* dt, int64_t n,
@@ -591,7 +687,9 @@ int runMapDev(const Module& m, void* const* bufs, const int32_t* dt, int64_t n,
         void* a = root.a >= 0 ? offsetPtr(bufAt(bufs, m, root.a), root.begin, dtOut) : nullptr;
         void* b = root.b >= 0 ? offsetPtr(bufAt(bufs, m, root.b), root.begin, dtOut) : nullptr;
         int st = MLKB_OK;
-        if (l.kernel == kMapSinDsin) {
+        if (l.kernel == kMapChains) {
+            st = runChainGroup(m, l, bufs, dt, a, b, cnt, scalars, n_scalars, stream);
+        } else if (l.kernel == kMapSinDsin) {
             void* dy = offsetPtr(bufAt(bufs, m, m.roots[l.q].out), root.begin, dtOut);
             st = mlkb_map_sin_dsin_f32(static_cast<const float*>(a), static_cast<float*>(out),
                                        static_cast<float*>(dy), cnt, stream);
@@ -619,6 +717,10 @@ std::string planText(const Module& m, const int32_t* dt) {
     switch (m.kind) {
         case MLKB_KIND_MAP:
             for (const MapLaunch& l : planMap(m, dt)) {
+                if (l.kernel == kMapChains) {
+                    add(("map_chains" + std::to_string(l.group.size())).c_str());
+                    continue;
+                }
                 add(l.kernel == kMapSinDsin ? "map_sin_dsin_f32"
                     : l.kernel == kMapSin   ? "map_sin_f32"
                     : (m.roots[l.r].poly7 ? "map_chain_poly7" : "map_chain"));

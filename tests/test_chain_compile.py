@@ -78,3 +78,37 @@ def test_bad_chains_refused_before_compiling():
         api.chain_build(kir.chain(E("mul", A, B)), has_b=False)
     _, after, _ = api.chain_compile(-1)
     assert after == before
+
+
+def _plan(chains, **kw):
+    m = api.Module(kir.map_module(chains, **kw))
+    return m.plan([mb.F64 if kw.get("dtype") == "f64" else mb.F32] * m.num_buffers)
+
+
+def test_roots_over_the_same_inputs_share_one_kernel():
+    two_x = kir.chain(E("mul", A, C(2.0)))
+    cube = kir.chain(E("mul", A, A), E("mul", T(0), A))
+    # no dedicated kernel applies (poly7 family): one kernel for all three roots
+    assert _plan([kir.SIN_CHAIN, kir.DSIN_CHAIN, two_x], poly7=True) == "map_chains3"
+    # the dedicated pair stays; the other roots are grouped
+    assert _plan([kir.SIN_CHAIN, kir.DSIN_CHAIN, two_x, cube]) == "map_sin_dsin_f32,map_chains2"
+    # at most 8 roots per kernel
+    assert _plan([two_x] * 10) == "map_chains8,map_chains2"
+    # two inputs
+    ab = kir.chain(E("mul", A, B))
+    assert _plan([ab, ab, two_x], n_inputs=2, dtype="f64") == "map_chains3"
+
+
+def test_roots_that_cannot_share_a_kernel():
+    two_x = kir.chain(E("mul", A, C(2.0)))
+    # a root that overwrites the input: the next root must see the new values
+    mod = kir.map_module([two_x, two_x])
+    mod["nodes"][2]["out"] = 0
+    m = api.Module(mod)
+    assert m.plan([mb.F32] * m.num_buffers) == "map_chain,map_chain"
+    # different ranges
+    mod = kir.map_module([two_x, two_x])
+    for node in mod["nodes"][3:]:
+        node["end"] = 100
+    m = api.Module(mod)
+    assert m.plan([mb.F32] * m.num_buffers) == "map_chain,map_chain"

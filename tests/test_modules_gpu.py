@@ -202,3 +202,47 @@ def test_compiled_chain_reused_across_constants_and_scalars(cuda):
         assert same_bits(host(y), want), v
     _, c1, _ = api.chain_compile(-1)
     assert c1 - c0 <= 1, (c0, c1)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f64"])
+def test_root_group_runs_as_one_kernel(cuda, dtype, chain_path):
+    # four roots no dedicated kernel matches (the poly7 family), one input:
+    # compiled, ONE kernel writes all four outputs, each bit-identical to the
+    # root run on its own; interpreted, the roots run one by one (the counter
+    # counts compiled launches only)
+    E, A, C, T = kir.E, kir.A, kir.C, kir.T
+    chains = [kir.SIN_CHAIN, kir.DSIN_CHAIN, kir.chain(E("mul", A, C(2.0))),
+              kir.chain(E("mul", A, A), E("mul", T(0), A))]
+    m = api.Module(kir.map_module(chains, poly7=True, dtype=dtype))
+    tdt = cuda.float32 if dtype == "f32" else cuda.float64
+    assert m.plan([mb.F32 if dtype == "f32" else mb.F64] * m.num_buffers) == "map_chains4"
+    n = 100003
+    x = dev(cuda, np.linspace(-7.0, 7.0, n).astype(np.float32 if dtype == "f32" else np.float64))
+    outs = [empty(cuda, (n,), tdt) for _ in chains]
+    _, _, before = api.chain_compile(-1)
+    m.run_dev([x] + outs, n=n)
+    cuda.cuda.synchronize()
+    _, _, after = api.chain_compile(-1)
+    assert after - before == (1 if chain_path == "compiled" else 0)  # compiled launches
+    for ch, o in zip(chains, outs):
+        want = empty(cuda, (n,), tdt)
+        api.map_chain(ch, x, want, poly7=True)
+        assert same_bits(host(o), host(want))
+
+
+def test_two_input_group_through_the_reference_abi(cuda):
+    # f64 host buffers through mlk_kernel; the roots share x and w, one root
+    # reads only x; arithmetic chains are bit-exact against the executor
+    E, A, B, C, T = kir.E, kir.A, kir.B, kir.C, kir.T
+    chains = [kir.chain(E("mul", A, B)), kir.chain(E("mul", A, B), E("sub", T(0), A)),
+              kir.chain(E("mul", A, C(2.0)))]
+    mod = kir.map_module(chains, n_inputs=2, dtype="f64")
+    assert api.Module(mod).plan([mb.F64] * 5) == "map_chains3"
+    n = 70001
+    rng = np.random.default_rng(11)
+    x, w = rng.normal(0, 3, n), rng.normal(0, 3, n)
+    outs = [np.zeros(n) for _ in chains]
+    assert api.legacy_call(mod, [x, w] + outs, n) == 0
+    for ch, o in zip(chains, outs):
+        (want,) = oracle.port().chain([ch], x, w)
+        assert np.array_equal(o, want)

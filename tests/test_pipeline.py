@@ -32,9 +32,10 @@ def test_pipeline_modules_take_the_dedicated_kernels(golden):
     assert plans["both"] == "map_sin_dsin_f32"
     assert plans["dsin"] == "map_chain"     # a derivative alone has no dedicated kernel
     assert plans["scalar"] == "map_chain"   # x as a ScalarParam: a one-element chain
-    # the reference ABI is f64 end to end: the generic chain, bit-exact arithmetic
+    # the reference ABI is f64 end to end: the generic chain path, both roots
+    # in one kernel (they read the same x over the same range)
     both = api.Module(m["both"])
-    assert both.plan([mb.F64] * 3) == "map_chain,map_chain"
+    assert both.plan([mb.F64] * 3) == "map_chains2"
 
 
 def test_pipeline_derivative_is_the_hand_chain(golden):

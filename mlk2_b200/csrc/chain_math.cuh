@@ -153,27 +153,22 @@ enum : unsigned char { kConst = 0, kElemA, kElemB, kScalar, kTemp };
 // same correctly rounded operation in the same order (__d*_rn, no FMA), so
 // the result is bit-identical. The coefficients are the reference's own
 // published constants (math_families.h:30-35, :49-54).
-__device__ __forceinline__ double poly7_sin_reduced(double x) {
+// The sine (cosine = false) or cosine residual polynomial of the poly7
+// family for the reduced argument x, as one chain of the same correctly
+// rounded steps with per-element coefficient selects, so lanes of a warp in
+// different quadrants run one path: sine x + (x*r2)*p, cosine
+// (1 - r2*0.5) + (r2*r2)*p, each p a 6-coefficient Horner chain in r2.
+__device__ __forceinline__ double poly7_residual(double x, bool cosine) {
     const double r2 = __dmul_rn(x, x);
-    double p = 1.58962301576546568060e-10;
-    p = __dadd_rn(__dmul_rn(p, r2), -2.50507477628578072866e-8);
-    p = __dadd_rn(__dmul_rn(p, r2), 2.75573136213857245213e-6);
-    p = __dadd_rn(__dmul_rn(p, r2), -1.98412698295895385996e-4);
-    p = __dadd_rn(__dmul_rn(p, r2), 8.33333333332211858878e-3);
-    p = __dadd_rn(__dmul_rn(p, r2), -1.66666666666666307295e-1);
-    return __dadd_rn(x, __dmul_rn(__dmul_rn(x, r2), p));  // x + x*r2*p, left to right
-}
-
-__device__ __forceinline__ double poly7_cos_reduced(double x) {
-    const double r2 = __dmul_rn(x, x);
-    double p = -1.13585365213876817300e-11;
-    p = __dadd_rn(__dmul_rn(p, r2), 2.08757530072652689750e-9);
-    p = __dadd_rn(__dmul_rn(p, r2), -2.75573142103085808917e-7);
-    p = __dadd_rn(__dmul_rn(p, r2), 2.48015872890001867312e-5);
-    p = __dadd_rn(__dmul_rn(p, r2), -1.38888888888783992457e-3);
-    p = __dadd_rn(__dmul_rn(p, r2), 4.16666666666666435770e-2);
-    // 1 - r2*0.5 + r2*r2*p, left to right
-    return __dadd_rn(__dsub_rn(1.0, __dmul_rn(r2, 0.5)), __dmul_rn(__dmul_rn(r2, r2), p));
+    double p = cosine ? -1.13585365213876817300e-11 : 1.58962301576546568060e-10;
+    p = __dadd_rn(__dmul_rn(p, r2), cosine ? 2.08757530072652689750e-9 : -2.50507477628578072866e-8);
+    p = __dadd_rn(__dmul_rn(p, r2), cosine ? -2.75573142103085808917e-7 : 2.75573136213857245213e-6);
+    p = __dadd_rn(__dmul_rn(p, r2), cosine ? 2.48015872890001867312e-5 : -1.98412698295895385996e-4);
+    p = __dadd_rn(__dmul_rn(p, r2), cosine ? -1.38888888888783992457e-3 : 8.33333333332211858878e-3);
+    p = __dadd_rn(__dmul_rn(p, r2), cosine ? 4.16666666666666435770e-2 : -1.66666666666666307295e-1);
+    const double head = cosine ? __dsub_rn(1.0, __dmul_rn(r2, 0.5)) : x;
+    const double scale = cosine ? __dmul_rn(r2, r2) : __dmul_rn(x, r2);
+    return __dadd_rn(head, __dmul_rn(scale, p));
 }
 
 __device__ __forceinline__ double poly7_sin(double x) {
@@ -181,19 +176,18 @@ __device__ __forceinline__ double poly7_sin(double x) {
     const double kPio2Lo = 6.1232339957367660359e-17;
     const double n = floor(__dadd_rn(__ddiv_rn(x, kPio2Hi), 0.5));
     const double r = __dsub_rn(__dsub_rn(x, __dmul_rn(n, kPio2Hi)), __dmul_rn(n, kPio2Lo));
-    // For x NaN or infinite, fmod(n, 4) is NaN and r is NaN. The reference
-    // converts that NaN to int (INT_MIN on its x86-64 host) and its switch
-    // takes the default branch, -cos(r): the same branch here keeps even the
-    // NaN's sign bit-identical.
-    const double f = fmod(n, 4.0);
+    // The reference takes fmod(n, 4) of the integer-valued n; every step of
+    // n - 4*trunc(n/4) is exact, so it is the same remainder (a zero may
+    // differ in sign, which does not change the quadrant). For x NaN or
+    // infinite it is NaN and r is NaN: the reference converts that NaN to
+    // int (INT_MIN on its x86-64 host) and its switch takes the default
+    // branch, -cos(r); the same branch here keeps even the NaN's sign
+    // bit-identical.
+    const double f = n - 4.0 * trunc(n * 0.25);
     int q = (f == f) ? static_cast<int>(f) : 3;
     if (q < 0) q += 4;
-    switch (q) {
-        case 0: return poly7_sin_reduced(r);
-        case 1: return poly7_cos_reduced(r);
-        case 2: return -poly7_sin_reduced(r);
-        default: return -poly7_cos_reduced(r);
-    }
+    const double v = poly7_residual(r, (q & 1) != 0);  // quadrants 1, 3: cosine
+    return q >= 2 ? -v : v;
 }
 
 // kF64Out: the chain result is stored in f64, so sin/cos use CUDA's double

@@ -211,22 +211,29 @@ int mlkb_module_run_host(const mlkb_module* module, void* const* bufs,
                          const double* scalars, int64_t n_scalars,
                          int32_t n_gpus);
 
-/* Flag of mlkb_module_run_sharded: assemble every output on device 0. */
+/* Flags of mlkb_module_run_sharded: assemble every output on device 0; with
+ * it, move the shards by NCCL even where peer stores could (below). */
 #define MLKB_ASSEMBLE_DEVICE0 1u
+#define MLKB_ASSEMBLE_VIA_NCCL 2u
 
 /*
  * The typed multi-GPU entry: runs the module sharded over devices
  * 0..n_gpus-1 (n_gpus <= 0: all visible devices) in contiguous element / row
  * / batch shards, inputs read from HOST buffers.
  *   flags 0                       outputs are host buffers: mlkb_module_run_host.
- *   flags MLKB_ASSEMBLE_DEVICE0   output buffers are DEVICE memory on device 0;
- *                                 each shard's part of every output is
- *                                 assembled there by grouped NCCL send/recv
- *                                 over NVLink (no kernel reads a peer's
- *                                 memory). Outputs a step reads back (MatMul's
- *                                 C, the composite's S, map outputs written in
- *                                 part) are first sent from device 0 to the
- *                                 shards the same way.
+ *   flags MLKB_ASSEMBLE_DEVICE0   output buffers are DEVICE memory on device 0.
+ *                                 Maps whose outputs no root reads, on devices
+ *                                 with peer access to device 0: each shard's
+ *                                 kernel stores its part of every output
+ *                                 straight into device 0's buffer over NVLink,
+ *                                 so computing and assembling are one pass (no
+ *                                 kernel loads a peer's memory). Otherwise, or
+ *                                 with MLKB_ASSEMBLE_VIA_NCCL as well, every
+ *                                 shard's part is assembled by grouped NCCL
+ *                                 send/recv, and outputs a step reads back
+ *                                 (MatMul's C, the composite's S, map outputs
+ *                                 written in part) are first sent from device
+ *                                 0 to the shards the same way.
  * NCCL is loaded on first use (libnccl.so.2, or the library named by the
  * environment variable MLKB_NCCL_LIB) and one communicator per device is kept
  * for the process; loading, communicator creation or a transfer failing

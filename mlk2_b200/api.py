@@ -14,6 +14,7 @@ import numpy as np
 from . import F16, F32, F64, check, kir, lib
 
 ASSEMBLE_DEVICE0 = 1  # MLKB_ASSEMBLE_DEVICE0
+ASSEMBLE_VIA_NCCL = 2  # MLKB_ASSEMBLE_VIA_NCCL
 
 _TORCH_DT = None
 
@@ -199,13 +200,16 @@ class Module:
         check(lib().mlkb_module_run_host(self._h, ptrs, dts, nb, n, sc, len(scalars), n_gpus))
 
     def run_sharded(self, bufs, n: int = 0, scalars: Sequence[float] = (), n_gpus: int = 0,
-                    assemble: bool = True) -> int:
+                    assemble: bool = True, via_nccl: bool = False) -> int:
         """Inputs from host buffers, sharded over n_gpus devices; with
-        `assemble` the outputs are device-0 tensors filled by NCCL. Returns
-        the status (0 = ok) rather than raising, for fault-injection tests."""
+        `assemble` the outputs are device-0 tensors, filled by the shards'
+        peer stores (maps) or by NCCL (other kinds, or with `via_nccl`).
+        Returns the status (0 = ok) rather than raising, for fault-injection
+        tests."""
         ptrs, dts, nb, sc = self._args(bufs, scalars)
+        flags = (ASSEMBLE_DEVICE0 | (ASSEMBLE_VIA_NCCL if via_nccl else 0)) if assemble else 0
         return lib().mlkb_module_run_sharded(self._h, ptrs, dts, nb, n, sc, len(scalars), n_gpus,
-                                             ASSEMBLE_DEVICE0 if assemble else 0)
+                                             flags)
 
 
 def legacy_call(module: dict, host_f64: Sequence[np.ndarray], n: int,

@@ -58,12 +58,16 @@ __device__ __forceinline__ double u_of(float x) {
     return fma(3.0, xd, xd * xd);
 }
 
-// |x| < 1000 for all four lanes keeps |u| < 2^20, the range of the two-term
-// reduction. A NaN lane is ignored by the max and takes the fast path, whose
-// arithmetic carries the NaN through to both outputs; inf fails the test.
+// |x| < 1000 keeps |u| < 2^20, the range of the two-term reduction. A NaN
+// takes the fast path, whose arithmetic carries the NaN through to both
+// outputs; inf and |x| >= 1000 take the slow one. The choice is made per
+// element, so an element's result never depends on its neighbours or on the
+// buffers' alignment (a shard boundary or an unaligned buffer gives the same
+// bits as the vector path).
+__device__ __forceinline__ bool fast_elem(float x) { return !(fabsf(x) >= 1000.0f); }
+
 __device__ __forceinline__ bool fast_range(float4 v) {
-    const float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    return m < 1000.0f;
+    return fast_elem(v.x) && fast_elem(v.y) && fast_elem(v.z) && fast_elem(v.w);
 }
 
 // Sign bit 31 set when bit 1 of q is: the quadrant's sign flip, applied to the
@@ -139,6 +143,18 @@ struct SinDsinOp {
     }
 };
 
+// One element, the path fast_elem picks for it.
+template <class Op>
+__device__ __forceinline__ void eval1(float x, float& o0, float& o1) {
+    if (fast_elem(x)) {
+        Op::fast(x, o0, o1);
+    } else {
+        const float2 r = Op::slow(x);
+        o0 = r.x;
+        o1 = r.y;
+    }
+}
+
 template <class Op>
 __device__ __forceinline__ void eval4(float4 v, float4& o0, float4& o1) {
     if (fast_range(v)) {
@@ -146,10 +162,11 @@ __device__ __forceinline__ void eval4(float4 v, float4& o0, float4& o1) {
         Op::fast(v.y, o0.y, o1.y);
         Op::fast(v.z, o0.z, o1.z);
         Op::fast(v.w, o0.w, o1.w);
-    } else {  // NaN, inf or |x| >= 1000 somewhere in the vector
-        const float2 a = Op::slow(v.x), b = Op::slow(v.y), c = Op::slow(v.z), d = Op::slow(v.w);
-        o0 = make_float4(a.x, b.x, c.x, d.x);
-        o1 = make_float4(a.y, b.y, c.y, d.y);
+    } else {  // inf or |x| >= 1000 somewhere in the vector: each lane on its own
+        eval1<Op>(v.x, o0.x, o1.x);
+        eval1<Op>(v.y, o0.y, o1.y);
+        eval1<Op>(v.z, o0.z, o1.z);
+        eval1<Op>(v.w, o0.w, o1.w);
     }
 }
 
@@ -197,16 +214,18 @@ map_vec_kernel(const float4* __restrict__ x, float4* __restrict__ y0,
     }
 }
 
-// Scalar body for the ragged tail or unaligned pointers.
+// Scalar body for the ragged tail or unaligned pointers (per element the same
+// arithmetic as the vector body).
 template <class Op>
 __global__ void map_scalar_kernel(const float* __restrict__ x, float* __restrict__ y0,
                                   float* __restrict__ y1, int64_t begin, int64_t n) {
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t i = begin + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
          i < n; i += stride) {
-        const float2 o = Op::slow(x[i]);
-        y0[i] = o.x;
-        if (Op::kOuts > 1) y1[i] = o.y;
+        float o0, o1 = 0.0f;
+        eval1<Op>(x[i], o0, o1);
+        y0[i] = o0;
+        if (Op::kOuts > 1) y1[i] = o1;
     }
 }
 

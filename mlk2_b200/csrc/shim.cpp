@@ -1385,8 +1385,41 @@ ShardPlan planShard(const Module& m0, const Shard& sh, int64_t n) {
     return p;
 }
 
+// Peer access from device d to device 0 (enabled once per process and kept):
+// true when d's kernels may store into device 0's memory.
+bool peerToDevice0(int d) {
+    static std::atomic<int> state[64];  // 0 unknown, 1 yes, 2 no
+    if (d == 0) return true;
+    if (d < 0 || d >= 64) return false;
+    if (state[d] == 0) {
+        int can = 0;
+        bool ok = cudaDeviceCanAccessPeer(&can, d, 0) == cudaSuccess && can != 0;
+        if (ok && cudaSetDevice(d) == cudaSuccess) {
+            const cudaError_t e = cudaDeviceEnablePeerAccess(0, 0);
+            ok = e == cudaSuccess || e == cudaErrorPeerAccessAlreadyEnabled;
+        }
+        cudaGetLastError();
+        state[d] = ok ? 1 : 2;
+    }
+    return state[d] == 1;
+}
+
+// A map whose every output is only written (no root reads a buffer any root
+// writes): its shards can store straight into device 0's outputs, and a root
+// writing only part of an output leaves the rest of device 0's buffer as it
+// was, which is what the executor leaves.
+bool writeOnlyOutputs(const Module& m) {
+    if (m.kind != MLKB_KIND_MAP) return false;
+    for (const MapRoot& r : m.roots) {
+        for (const MapRoot& o : m.roots) {
+            if (o.out == r.a || o.out == r.b) return false;
+        }
+    }
+    return true;
+}
+
 int runAssembled(const Module& m, void* const* bufs, const int32_t* dt, int32_t n_bufs, int64_t n,
-                 const double* scalars, int64_t n_scalars, int32_t n_gpus) {
+                 const double* scalars, int64_t n_scalars, int32_t n_gpus, bool viaNccl) {
     if (n_bufs != static_cast<int32_t>(m.bindable.size())) {
         return setError(MLKB_ERR_INVALID, "run_sharded: buffer count differs from the module table");
     }
@@ -1435,12 +1468,21 @@ int runAssembled(const Module& m, void* const* bufs, const int32_t* dt, int32_t 
     const cudaStream_t s0 = g_dev[0].streams[0];
     cudaError_t e = cudaSuccess;
     auto bytes = [&](size_t i, const BufPlan& b) { return static_cast<size_t>(b.cnt) * elemBytes(dt[i]); };
+    // Peer stores: every shard writes its part of each output into device 0's
+    // buffer itself (maps only; see writeOnlyOutputs), no transfer step.
+    bool peer = !viaNccl && writeOnlyOutputs(m);
+    for (const ShardPlan& p : plans) peer = peer && peerToDevice0(p.dev);
     // 1. slots and host inputs
     for (ShardPlan& p : plans) {
         cudaSetDevice(p.dev);
         p.st = g_dev[p.dev].streams[0];
         for (size_t i = 0; i < p.b.size(); ++i) {
             BufPlan& b = p.b[i];
+            if (peer && m.buffers[m.bindable[i]].output) {
+                b.slot = offsetPtr(bufs[i], b.off, dt[i]);  // device 0's own buffer
+                b.rmw = b.out = false;                       // nothing to move
+                continue;
+            }
             if (int st = slotPtr(p.dev, i, bytes(i, b), &b.slot)) return st;
             if (b.in && b.cnt > 0) {
                 e = cudaMemcpyAsync(b.slot, offsetPtr(bufs[i], b.off, dt[i]), bytes(i, b),
@@ -1614,13 +1656,18 @@ extern "C" int mlkb_module_run_sharded(const mlkb_module* module, void* const* b
         return setError(MLKB_ERR_INVALID, "run_sharded: null argument");
     }
     if (n < 0) return setError(MLKB_ERR_INVALID, "run_sharded: negative element count");
-    if ((flags & ~static_cast<uint32_t>(MLKB_ASSEMBLE_DEVICE0)) != 0) {
+    if ((flags & ~static_cast<uint32_t>(MLKB_ASSEMBLE_DEVICE0 | MLKB_ASSEMBLE_VIA_NCCL)) != 0) {
         return setError(MLKB_ERR_INVALID, "run_sharded: unknown flag");
     }
     if ((flags & MLKB_ASSEMBLE_DEVICE0) == 0) {
+        if ((flags & MLKB_ASSEMBLE_VIA_NCCL) != 0) {
+            return setError(MLKB_ERR_INVALID,
+                            "run_sharded: MLKB_ASSEMBLE_VIA_NCCL needs MLKB_ASSEMBLE_DEVICE0");
+        }
         return runHost(module->m, bufs, dtypes, n_bufs, n, scalars, n_scalars, n_gpus);
     }
-    return runAssembled(module->m, bufs, dtypes, n_bufs, n, scalars, n_scalars, n_gpus);
+    return runAssembled(module->m, bufs, dtypes, n_bufs, n, scalars, n_scalars, n_gpus,
+                        (flags & MLKB_ASSEMBLE_VIA_NCCL) != 0);
 }
 
 extern "C" int mlk_bind_module(const char* json) {

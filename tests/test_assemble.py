@@ -1,11 +1,13 @@
-"""Sharded runs assembled on device 0 with NCCL (mlkb_module_run_sharded).
+"""Sharded runs assembled on device 0 (mlkb_module_run_sharded): maps by the
+shards' own peer stores into device 0's buffers, the other kinds (and maps
+with MLKB_ASSEMBLE_VIA_NCCL) by NCCL.
 
 CPU part: NCCL that cannot be loaded, or lacks its entry points, is reported
 as MLKB_ERR_NCCL (code 5) before any device is touched. GPU part: an NCCL
 whose communicator creation fails (a stand-in library built here) is
-reported the same way with the outputs untouched; with the real NCCL the
-assembled outputs are bit-identical to the host-buffer run, on one GPU and
-on every GPU of the box.
+reported the same way with the outputs untouched; otherwise the assembled
+outputs are bit-identical to the host-buffer run, on one GPU and on every
+GPU of the box, by either transfer.
 """
 import os
 import subprocess
@@ -59,6 +61,9 @@ def test_unknown_flag_rejected():
     ptrs, dts, nb, sc = m._args([x, y, y.copy()], [])
     assert mb.lib().mlkb_module_run_sharded(m._h, ptrs, dts, nb, x.size, sc, 0, 1, 6) == \
         mb.ERR_INVALID
+    # the NCCL-only flag means nothing without assembly
+    assert mb.lib().mlkb_module_run_sharded(m._h, ptrs, dts, nb, x.size, sc, 0, 1, 2) == \
+        mb.ERR_INVALID
 
 
 @pytest.mark.gpu
@@ -79,6 +84,11 @@ def _cases(cuda):
     x = rng.uniform(-8, 8, 100003).astype(np.float32)
     yield "map", kir.map_module([kir.SIN_CHAIN, kir.DSIN_CHAIN]), [x], [(x.size,)] * 2, x.size, \
         np.float32
+    # a root that writes only part of its output, next to a full one: the rest
+    # of device 0's buffer keeps its values
+    part = kir.map_module([kir.SIN_CHAIN, kir.chain(kir.E("mul", kir.A, kir.C(2.0)))])
+    part["nodes"][0]["end"] = 60000
+    yield "map_part", part, [x], [(x.size,)] * 2, x.size, np.float32
     # softmax rows
     a = rng.normal(0, 4, (1000, 512)).astype(np.float32)
     yield "softmax", kir.call_module("softmax", 1000, 512), [a], [(1000, 512)], 0, np.float32
@@ -95,8 +105,11 @@ def _cases(cuda):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("via_nccl", [False, True])
 @pytest.mark.parametrize("n_gpus", [1, 0])
-def test_assembled_equals_host_run(cuda, monkeypatch, n_gpus):
+def test_assembled_equals_host_run(cuda, monkeypatch, n_gpus, via_nccl):
+    # maps assemble by the shards' peer stores into device 0 unless via_nccl;
+    # the other kinds always by NCCL. Same bits either way.
     monkeypatch.delenv("MLKB_NCCL_LIB", raising=False)
     for name, doc, ins, out_shapes, n, odt in _cases(cuda):
         m = api.Module(doc)
@@ -104,7 +117,7 @@ def test_assembled_equals_host_run(cuda, monkeypatch, n_gpus):
         host_outs = [o.copy() for o in start]
         m.run_host(ins + host_outs, n=n, n_gpus=1)
         dev_outs = [cuda.from_numpy(o.copy()).cuda() for o in start]
-        st = m.run_sharded(ins + dev_outs, n=n, n_gpus=n_gpus)
+        st = m.run_sharded(ins + dev_outs, n=n, n_gpus=n_gpus, via_nccl=via_nccl)
         assert st == 0, (name, mb.lib().mlkb_last_error().decode())
         for h, d in zip(host_outs, dev_outs):
             got = d.cpu().numpy()

@@ -222,13 +222,16 @@ int mlkb_module_run_host(const mlkb_module* module, void* const* bufs,
  * / batch shards, inputs read from HOST buffers.
  *   flags 0                       outputs are host buffers: mlkb_module_run_host.
  *   flags MLKB_ASSEMBLE_DEVICE0   output buffers are DEVICE memory on device 0.
- *                                 Maps whose outputs no root reads, on devices
- *                                 with peer access to device 0: each shard's
- *                                 kernel stores its part of every output
- *                                 straight into device 0's buffer over NVLink,
- *                                 so computing and assembling are one pass (no
- *                                 kernel loads a peer's memory). Otherwise, or
- *                                 with MLKB_ASSEMBLE_VIA_NCCL as well, every
+ *                                 Maps whose outputs no root reads, Softmax,
+ *                                 ReduceSum and the fused scaled-scores
+ *                                 composite, on devices with peer access to
+ *                                 device 0: each shard's kernel stores its
+ *                                 part of every output straight into device
+ *                                 0's buffer over NVLink, so computing and
+ *                                 assembling are one pass (no kernel loads a
+ *                                 peer's memory). Otherwise (MatMul, which
+ *                                 reads C back), or with
+ *                                 MLKB_ASSEMBLE_VIA_NCCL as well, every
  *                                 shard's part is assembled by grouped NCCL
  *                                 send/recv, and outputs a step reads back
  *                                 (MatMul's C, the composite's S, map outputs

@@ -1404,18 +1404,28 @@ bool peerToDevice0(int d) {
     return state[d] == 1;
 }
 
-// A map whose every output is only written (no root reads a buffer any root
-// writes): its shards can store straight into device 0's outputs, and a root
-// writing only part of an output leaves the rest of device 0's buffer as it
-// was, which is what the executor leaves.
+// Modules whose every output is only written, by kernels that store it with
+// plain stores: their shards can store straight into device 0's outputs.
+//  * maps where no root reads a buffer any root writes (a root writing only
+//    part of an output leaves the rest of device 0's buffer as it was, which
+//    is what the executor leaves);
+//  * Softmax and ReduceSum rows (Y written whole, A only read);
+//  * the fused scaled-scores composite (Y written whole; S and Sc are temps).
+// MatMul reads C back (C += A B), so it stays on the NCCL path.
 bool writeOnlyOutputs(const Module& m) {
-    if (m.kind != MLKB_KIND_MAP) return false;
-    for (const MapRoot& r : m.roots) {
-        for (const MapRoot& o : m.roots) {
-            if (o.out == r.a || o.out == r.b) return false;
-        }
+    switch (m.kind) {
+        case MLKB_KIND_MAP:
+            for (const MapRoot& r : m.roots) {
+                for (const MapRoot& o : m.roots) {
+                    if (o.out == r.a || o.out == r.b) return false;
+                }
+            }
+            return true;
+        case MLKB_KIND_SOFTMAX:
+        case MLKB_KIND_REDUCESUM: return m.callA != m.callOut;
+        case MLKB_KIND_QK_SOFTMAX: return m.qkFused;
+        default: return false;
     }
-    return true;
 }
 
 int runAssembled(const Module& m, void* const* bufs, const int32_t* dt, int32_t n_bufs, int64_t n,
@@ -1469,7 +1479,7 @@ int runAssembled(const Module& m, void* const* bufs, const int32_t* dt, int32_t 
     cudaError_t e = cudaSuccess;
     auto bytes = [&](size_t i, const BufPlan& b) { return static_cast<size_t>(b.cnt) * elemBytes(dt[i]); };
     // Peer stores: every shard writes its part of each output into device 0's
-    // buffer itself (maps only; see writeOnlyOutputs), no transfer step.
+    // buffer itself (see writeOnlyOutputs), no transfer step.
     bool peer = !viaNccl && writeOnlyOutputs(m);
     for (const ShardPlan& p : plans) peer = peer && peerToDevice0(p.dev);
     // 1. slots and host inputs

@@ -268,6 +268,54 @@ struct Compiled {
 std::mutex g_cacheMu;
 std::unordered_map<std::string, std::unique_ptr<Compiled>> g_cache;
 
+// A group's structure as a compact byte string (everything generate() turns
+// into source text except the constants' values), so a repeated launch finds
+// its kernel without generating the source again.
+struct Known {
+    Compiled* c;
+    bool usesA, usesB;
+};
+std::unordered_map<std::string, Known> g_known;  // guarded by g_cacheMu
+
+std::string structKey(const JitExpr* const* chains, const int* ns, const bool* poly7, int nChains,
+                      bool f64) {
+    std::string k;
+    k.reserve(16 + 8 * 64);
+    k.push_back(static_cast<char>(f64 ? 1 : 0));
+    k.push_back(static_cast<char>(nChains));
+    for (int j = 0; j < nChains; ++j) {
+        k.push_back(static_cast<char>(poly7[j] ? 1 : 0));
+        k.push_back(static_cast<char>(ns[j]));
+        for (int e = 0; e < ns[j]; ++e) {
+            const JitExpr& x = chains[j][e];
+            const bool tempA = x.akind == chain::kTemp, tempB = x.bkind == chain::kTemp;
+            k.push_back(static_cast<char>(x.op));
+            k.push_back(static_cast<char>(x.unary));
+            k.push_back(static_cast<char>(x.akind));
+            k.push_back(static_cast<char>(tempA ? x.aidx : 0));
+            k.push_back(static_cast<char>(x.unary ? 0 : x.bkind));
+            k.push_back(static_cast<char>(!x.unary && tempB ? x.bidx : 0));
+        }
+    }
+    return k;
+}
+
+// The constants of a group in generate()'s numbering: operand order, chain
+// by chain (every operand that is not ElemA, ElemB or a temp; a unary op's
+// second operand is not an operand).
+void constsOf(const JitExpr* const* chains, const int* ns, int nChains, std::vector<double>& v) {
+    auto take = [&](int kind, double val) {
+        if (kind != chain::kElemA && kind != chain::kElemB && kind != chain::kTemp) v.push_back(val);
+    };
+    for (int j = 0; j < nChains; ++j) {
+        for (int e = 0; e < ns[j]; ++e) {
+            const JitExpr& x = chains[j][e];
+            take(x.akind, x.aval);
+            if (!x.unary) take(x.bkind, x.bval);
+        }
+    }
+}
+
 void compileInto(const std::string& src, Compiled& c) {
     const NvrtcApi& api = nvrtc();
     nvrtcProgram prog = nullptr;
@@ -321,9 +369,21 @@ int launchChainsJit(const JitExpr* const* chains, const int* n_exprs, const bool
         return kJitUnavailable;
     }
     const bool f64 = dtype == MLKB_F64;
-    Generated g = generate(chains, n_exprs, poly7, n_chains, f64);
-    if ((g.usesA && a == nullptr) || (g.usesB && b == nullptr)) return kJitUnavailable;
-    Compiled* c = entryFor(g.src);
+    const std::string key = structKey(chains, n_exprs, poly7, n_chains, f64);
+    Known known{nullptr, false, false};
+    {
+        std::lock_guard<std::mutex> lk(g_cacheMu);
+        auto it = g_known.find(key);
+        if (it != g_known.end()) known = it->second;
+    }
+    if (known.c == nullptr) {  // first launch of this structure: generate, compile
+        Generated g = generate(chains, n_exprs, poly7, n_chains, f64);
+        known = Known{entryFor(g.src), g.usesA, g.usesB};
+        std::lock_guard<std::mutex> lk(g_cacheMu);
+        g_known.emplace(key, known);
+    }
+    Compiled* c = known.c;
+    if ((known.usesA && a == nullptr) || (known.usesB && b == nullptr)) return kJitUnavailable;
     if (!c->error.empty()) return kJitUnavailable;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
@@ -367,7 +427,8 @@ int launchChainsJit(const JitExpr* const* chains, const int* n_exprs, const bool
     const int64_t cap = static_cast<int64_t>(smCount()) * per;
     const int grid = static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
 
-    std::vector<double> consts = g.consts;
+    std::vector<double> consts;
+    constsOf(chains, n_exprs, n_chains, consts);
     if (consts.empty()) consts.push_back(0.0);
     long long nn = n;
     int vflag = vec ? 1 : 0;

@@ -100,8 +100,8 @@ def poly_bench(tmp_path, suites):
                MLK_BACKEND_WORKDIR=str(tmp_path))
     out_json = tmp_path / "rows.json"
     subprocess.run([POLY, "bench", "--reps=3", "--warmup=1", f"--suites={suites}",
-                    f"--json-out={out_json}"], env=env, capture_output=True, text=True,
-                   timeout=900)
+                    "--b200-max-ulp=8", f"--json-out={out_json}"], env=env,
+                   capture_output=True, text=True, timeout=900)
     return json.loads(out_json.read_text())["rows"]
 
 
@@ -121,7 +121,7 @@ def test_poly_bench_b200_rows(cuda, tmp_path):
     tier1 = {(r["suite"], r["shape"]) for r in rows if r["path"] == "tier1" and r["timed"]}
     assert set(b200) == tier1 and ("gemm", "1024x1024x1024") in b200
     for key, r in b200.items():
-        assert r["timed"], (key, r["note"])
+        assert r["timed"] and r["within_bound"], (key, r["note"])   # the table's OK
         if key[0] in ("gemm", "reducesum"):
             assert r["bitexact"] and r["note"] == "bit-exact", (key, r)
         else:  # f64 softmax: only CUDA's exp differs from the host libm's

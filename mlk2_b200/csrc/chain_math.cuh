@@ -24,22 +24,30 @@ __device__ __forceinline__ double reduce_pio2(double u, int& q) {
 }
 
 // sin and cos of the reduced argument |r| <= pi/4 (+ a rounding margin),
-// Taylor series through r^11 (sin) and r^12 (cos), Horner form in f64.
-// Truncation error < 1e-11 relative, far below f32 resolution.
+// Taylor series through r^17 (sin) and r^16 (cos), Horner form in f64:
+// truncation below 1e-19 / 3e-18, so both are accurate to about an f64 ulp,
+// as the host libm the reference calls is. (A value that later cancels
+// against a nearby constant in a chain must be as accurate as the
+// reference's, or the cancellation magnifies the difference.)
 __device__ __forceinline__ double sin_poly(double r, double z) {
-    double p = -2.505210838544172e-08;   // -1/11!
-    p = fma(z, p, 2.7557319223985893e-06);  // 1/9!
-    p = fma(z, p, -1.984126984126984e-04); // -1/7!
-    p = fma(z, p, 8.333333333333333e-03);  // 1/5!
-    p = fma(z, p, -1.6666666666666666e-01); // -1/3!
+    double p = 2.8114572543455206e-15;     // 1/17!
+    p = fma(z, p, -7.647163731819816e-13);   // -1/15!
+    p = fma(z, p, 1.6059043836821613e-10);   // 1/13!
+    p = fma(z, p, -2.505210838544172e-08);   // -1/11!
+    p = fma(z, p, 2.7557319223985893e-06);   // 1/9!
+    p = fma(z, p, -1.984126984126984e-04);   // -1/7!
+    p = fma(z, p, 8.333333333333333e-03);    // 1/5!
+    p = fma(z, p, -1.6666666666666666e-01);  // -1/3!
     return fma(r * z, p, r);
 }
 
 __device__ __forceinline__ double cos_poly(double z) {
-    double p = 2.08767569878681e-09;     // 1/12!
-    p = fma(z, p, -2.755731922398589e-07);  // -1/10!
-    p = fma(z, p, 2.48015873015873e-05);   // 1/8!
-    p = fma(z, p, -1.388888888888889e-03);  // -1/6!
+    double p = 4.779477332387385e-14;      // 1/16!
+    p = fma(z, p, -1.1470745597729725e-11);  // -1/14!
+    p = fma(z, p, 2.08767569878681e-09);     // 1/12!
+    p = fma(z, p, -2.755731922398589e-07);   // -1/10!
+    p = fma(z, p, 2.48015873015873e-05);     // 1/8!
+    p = fma(z, p, -1.388888888888889e-03);   // -1/6!
     p = fma(z, p, 4.1666666666666664e-02);   // 1/4!
     p = fma(z, p, -0.5);
     return fma(z, p, 1.0);
@@ -66,12 +74,13 @@ __device__ __forceinline__ void sincos_f64(double u, double& s, double& c) {
 
 // sin_poly(r, z) when `cosine` is false, cos_poly(z) when it is true, as one
 // Horner chain whose coefficients are selected per element, so a warp whose
-// lanes need different polynomials runs one chain instead of both. The
-// result is bit-identical to calling the chosen function: the sine chain is
-// given a leading zero coefficient, and fma(z, 0, s) = s exactly for the
-// finite z = r*r of a reduced argument.
+// lanes need different polynomials runs one chain instead of both. Both have
+// eight coefficients, so the result is bit-identical to calling the chosen
+// function.
 __device__ __forceinline__ double sin_or_cos_poly(double r, double z, bool cosine) {
-    double p = cosine ? 2.08767569878681e-09 : 0.0;
+    double p = cosine ? 4.779477332387385e-14 : 2.8114572543455206e-15;
+    p = fma(z, p, cosine ? -1.1470745597729725e-11 : -7.647163731819816e-13);
+    p = fma(z, p, cosine ? 2.08767569878681e-09 : 1.6059043836821613e-10);
     p = fma(z, p, cosine ? -2.755731922398589e-07 : -2.505210838544172e-08);
     p = fma(z, p, cosine ? 2.48015873015873e-05 : 2.7557319223985893e-06);
     p = fma(z, p, cosine ? -1.388888888888889e-03 : -1.984126984126984e-04);

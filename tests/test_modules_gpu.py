@@ -246,3 +246,18 @@ def test_two_input_group_through_the_reference_abi(cuda):
     for ch, o in zip(chains, outs):
         (want,) = oracle.port().chain([ch], x, w)
         assert np.array_equal(o, want)
+
+
+def test_f32_chain_cancelling_after_sin_and_cos(cuda, chain_path):
+    # sin(x) - sin(pi/4) and cos(x) - cos(pi/4) for f32 x around pi/4: the
+    # results are tiny, so any error of sin / cos beyond f64 accuracy would
+    # show as many f32 ULPs; the reference's libm is accurate to an f64 ulp
+    E, A, C, T = kir.E, kir.A, kir.C, kir.T
+    xh = np.linspace(0.78, 0.79, 20011).astype(np.float32)
+    x = dev(cuda, xh)
+    for op in ("sin", "cos"):
+        ch = kir.chain(E(op, A), E("sub", T(0), C(0.7071067811865476)))
+        y = empty(cuda, x.shape, cuda.float32)
+        api.map_chain(ch, x, y)
+        (want,) = oracle.port().chain([ch], xh.astype(np.float64))
+        assert oracle.ulp_f32(host(y), want).max() <= 2, op

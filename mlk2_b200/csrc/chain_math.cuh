@@ -72,40 +72,60 @@ __device__ __forceinline__ void sincos_f64(double u, double& s, double& c) {
     }
 }
 
-// sin_poly(r, z) when `cosine` is false, cos_poly(z) when it is true, as one
-// Horner chain whose coefficients are selected per element, so a warp whose
-// lanes need different polynomials runs one chain instead of both. Both have
-// eight coefficients, so the result is bit-identical to calling the chosen
-// function.
-__device__ __forceinline__ double sin_or_cos_poly(double r, double z, bool cosine) {
-    double p = cosine ? 4.779477332387385e-14 : 2.8114572543455206e-15;
-    p = fma(z, p, cosine ? -1.1470745597729725e-11 : -7.647163731819816e-13);
-    p = fma(z, p, cosine ? 2.08767569878681e-09 : 1.6059043836821613e-10);
-    p = fma(z, p, cosine ? -2.755731922398589e-07 : -2.505210838544172e-08);
-    p = fma(z, p, cosine ? 2.48015873015873e-05 : 2.7557319223985893e-06);
-    p = fma(z, p, cosine ? -1.388888888888889e-03 : -1.984126984126984e-04);
-    p = fma(z, p, cosine ? 4.1666666666666664e-02 : 8.333333333333333e-03);
-    p = fma(z, p, cosine ? -0.5 : -1.6666666666666666e-01);
-    return fma(cosine ? z : r * z, p, cosine ? 1.0 : r);
+// sin(r) for |r| <= pi/2 (+ a rounding margin): the Taylor series through
+// r^21 (truncation below 2e-18), Horner form in f64.
+__device__ __forceinline__ double sin_half(double r) {
+    const double z = r * r;
+    double p = 1.9572941063391263e-20;       // 1/21!
+    p = fma(z, p, -8.22063524662433e-18);    // -1/19!
+    p = fma(z, p, 2.8114572543455206e-15);   // 1/17!
+    p = fma(z, p, -7.647163731819816e-13);   // -1/15!
+    p = fma(z, p, 1.6059043836821613e-10);   // 1/13!
+    p = fma(z, p, -2.505210838544172e-08);   // -1/11!
+    p = fma(z, p, 2.7557319223985893e-06);   // 1/9!
+    p = fma(z, p, -1.984126984126984e-04);   // -1/7!
+    p = fma(z, p, 8.333333333333333e-03);    // 1/5!
+    p = fma(z, p, -1.6666666666666666e-01);  // -1/3!
+    return fma(r * z, p, r);
 }
 
+// sin(u) alone, for |u| < 2^20: u = k*pi + r with |r| <= pi/2 and
+// sin(u) = (-1)^k sin(r). One odd series and a sign, no quadrant select: the
+// reduced argument is small exactly where sin(u) is, so the result keeps
+// its relative accuracy near the zeros. The first reduction step is exact
+// (for k != 0, |u| >= pi/2: u and k*fl(pi) are multiples of 2^-52 and their
+// difference is below 2); the second carries pi - fl(pi).
 __device__ __forceinline__ double sin_f64(double u) {
     if (fabs(u) < 1048576.0) {
-        int q;
-        const double r = reduce_pio2(u, q);
-        const double v = sin_or_cos_poly(r, r * r, (q & 1) != 0);
-        return (q & 2) ? -v : v;
+        const double kInvPi = 0.3183098861837907;      // fl64(1/pi)
+        const double kPiHi = 3.141592653589793;        // fl64(pi)
+        const double kPiLo = 1.2246467991473532e-16;   // fl64(pi - kPiHi)
+        const double kMagic = 6755399441055744.0;      // 1.5 * 2^52
+        const double t = fma(u, kInvPi, kMagic);
+        const double kd = t - kMagic;
+        const int k = __double2loint(t);
+        const double v = sin_half(fma(-kd, kPiLo, fma(-kd, kPiHi, u)));
+        return (k & 1) ? -v : v;
     }
     return ::sin(u);
 }
 
-// cos(u) alone: the same value as sincos_f64's c, with one polynomial.
+// cos(u) alone, for |u| < 2^20: u = (k + 1/2)*pi + r with |r| <= pi/2 (+ a
+// margin) and cos(u) = (-1)^(k+1) sin(r); r = u - m*pi/2 with m = 2k + 1,
+// in two steps as above (the first exact). Near the zeros of cos, r is small
+// and the result keeps its relative accuracy.
 __device__ __forceinline__ double cos_f64(double u) {
     if (fabs(u) < 1048576.0) {
-        int q;
-        const double r = reduce_pio2(u, q);
-        const double v = sin_or_cos_poly(r, r * r, (q & 1) == 0);
-        return ((q + 1) & 2) ? -v : v;
+        const double kInvPi = 0.3183098861837907;      // fl64(1/pi)
+        const double kP1 = 1.5707963267948966;         // fl64(pi/2)
+        const double kP2 = 6.123233995736766e-17;      // fl64(pi/2 - kP1)
+        const double kMagic = 6755399441055744.0;      // 1.5 * 2^52
+        const double t = fma(u, kInvPi, -0.5) + kMagic;  // rint(u/pi - 1/2), by rounding
+        const double kd = t - kMagic;
+        const int k = __double2loint(t);
+        const double m = fma(2.0, kd, 1.0);              // exact
+        const double v = sin_half(fma(-m, kP2, fma(-m, kP1, u)));
+        return (k & 1) ? v : -v;
     }
     double s, c;
     ::sincos(u, &s, &c);

@@ -44,7 +44,7 @@ const char kChainMathSrc[] =
     ;
 
 constexpr int kJitThreads = 256;
-constexpr int kJitUnroll = 2;  // 16-byte vectors in flight per thread
+constexpr int kJitUnroll = 1;  // 16-byte vectors per thread per step (1, 2 and 4 measured)
 
 // ---- NVRTC, loaded on first use ------------------------------------------------
 struct NvrtcApi {

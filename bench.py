@@ -8,7 +8,9 @@ f32, 2^28 elements per GPU (weak scaling: each rank owns a contiguous 2^28
 element shard of an N*2^28 element problem; no data-path collective). One
 step = one pass of the hot path over one shard; value = whole-job HBM GB/s
 at 12 algorithmic bytes per element. The other BASELINE configs (1, 3, 4,
-4', 5) are measured the same way and reported under "configs".
+4', 5) are measured the same way and reported under "configs", with a
+`chain` row: the generic chain path (compiled at run time) on the derivative
+chain the reference's calculus passes emit for config 2.
 
 Timing: W warm-up steps, then K steps bracketed by a barrier and a device
 synchronise, CUDA events on the launching stream, max over ranks. Inputs

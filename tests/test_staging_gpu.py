@@ -18,7 +18,8 @@ def _pinned(torch, a):
     return torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
 
 
-def test_map_pageable_equals_pinned_and_device(cuda):
+@pytest.mark.parametrize("n_gpus", [1, 0])        # 0: every GPU, shards staging at once
+def test_map_pageable_equals_pinned_and_device(cuda, n_gpus):
     n = 3 * (1 << 21) + 12345                      # two 2^22-element chunks, the last ragged
     xh = oracle.fill_uniform_f32(n, 5, 9, -8.0, 8.0)
     m = api.Module(kir.map_module([kir.SIN_CHAIN, kir.DSIN_CHAIN]))
@@ -27,15 +28,15 @@ def test_map_pageable_equals_pinned_and_device(cuda):
     want_y, want_dy = host(y0), host(dy0)
     for _ in range(2):                              # the second call reuses the staging
         y1, dy1 = np.full(n, np.nan, np.float32), np.full(n, np.nan, np.float32)
-        m.run_host([xh, y1, dy1], n=n, n_gpus=1)
+        m.run_host([xh, y1, dy1], n=n, n_gpus=n_gpus)
         assert np.array_equal(y1, want_y) and np.array_equal(dy1, want_dy)
     xp = _pinned(cuda, xh)
     yp, dyp = _pinned(cuda, np.full(n, np.nan, np.float32)), _pinned(cuda, np.full(n, np.nan, np.float32))
-    m.run_host([xp, yp, dyp], n=n, n_gpus=1)
+    m.run_host([xp, yp, dyp], n=n, n_gpus=n_gpus)
     assert np.array_equal(yp.numpy(), want_y) and np.array_equal(dyp.numpy(), want_dy)
     # a pageable input with pinned outputs, and the reverse
     y2, dy2 = _pinned(cuda, np.zeros(n, np.float32)), np.zeros(n, np.float32)
-    m.run_host([xh, y2, dy2], n=n, n_gpus=1)
+    m.run_host([xh, y2, dy2], n=n, n_gpus=n_gpus)
     assert np.array_equal(y2.numpy(), want_y) and np.array_equal(dy2, want_dy)
 
 
@@ -64,7 +65,7 @@ def test_row_kinds_pageable_pieces(cuda):
     xs = (rng.standard_normal((4096, 4096)) * 4).astype(np.float32)
     sm = api.Module(kir.call_module("softmax", 4096, 4096))
     ys = np.full_like(xs, np.nan)
-    sm.run_host([xs, ys], n=0, n_gpus=1)
+    sm.run_host([xs, ys], n=0, n_gpus=0)           # row shards over every GPU
     yd = empty(cuda, xs.shape, cuda.float32)
     api.softmax(dev(cuda, xs), yd)
     assert np.array_equal(ys, host(yd))

@@ -288,6 +288,10 @@ int mlkb_map_chain(const mlkb_expr* exprs, int32_t n_exprs, int32_t poly7_sin,
 /* Run-time compilation of chains. mode 1 compiles chains on first use (the
  * default; MLKB_CHAIN_JIT=0 in the environment starts the process at 0),
  * 0 runs every chain on the interpreter, any other value changes nothing.
+ * With MLKB_CACHE_DIR set, compiled chains are also stored in that directory
+ * and later processes load them instead of compiling (nothing is written
+ * unless it is set; a stored file is used only when its recorded source
+ * equals the one wanted).
  * Returns 1 when chains will be compiled (mode 1 and NVRTC loadable), else 0;
  * *compiled and *launched (either may be NULL) receive how many chain
  * kernels this process has compiled and launched. No counterpart in the

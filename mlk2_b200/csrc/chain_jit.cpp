@@ -20,9 +20,12 @@
 // NVRTC is loaded with dlopen (MLKB_NVRTC_LIB, else libnvrtc.so.12): a host
 // without it runs every chain on the interpreter; nothing here is needed for
 // correctness. MLKB_CHAIN_JIT=0 in the environment, or mlkb_chain_compile(0,
-// ...), selects the interpreter.
+// ...), selects the interpreter. MLKB_CACHE_DIR keeps compiled chains on disk
+// for later processes (off unless set).
 #include <dlfcn.h>
 #include <nvrtc.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <atomic>
 #include <cstdio>
@@ -58,6 +61,7 @@ struct NvrtcApi {
     nvrtcResult (*logSize)(nvrtcProgram, size_t*) = nullptr;
     nvrtcResult (*log)(nvrtcProgram, char*) = nullptr;
     nvrtcResult (*destroy)(nvrtcProgram*) = nullptr;
+    nvrtcResult (*version)(int*, int*) = nullptr;
 };
 
 const NvrtcApi& nvrtc() {
@@ -84,7 +88,9 @@ const NvrtcApi& nvrtc() {
         a.logSize = reinterpret_cast<decltype(a.logSize)>(sym("nvrtcGetProgramLogSize"));
         a.log = reinterpret_cast<decltype(a.log)>(sym("nvrtcGetProgramLog"));
         a.destroy = reinterpret_cast<decltype(a.destroy)>(sym("nvrtcDestroyProgram"));
-        a.ok = a.create && a.compile && a.cubinSize && a.cubin && a.logSize && a.log && a.destroy;
+        a.version = reinterpret_cast<decltype(a.version)>(sym("nvrtcVersion"));
+        a.ok = a.create && a.compile && a.cubinSize && a.cubin && a.logSize && a.log && a.destroy &&
+               a.version;
         if (!a.ok) a.why = "NVRTC library lacks an entry point";
         return a;
     }();
@@ -316,8 +322,79 @@ void constsOf(const JitExpr* const* chains, const int* ns, int nChains, std::vec
     }
 }
 
+// ---- optional cache of compiled chains on disk ------------------------------------
+// With MLKB_CACHE_DIR set, every compiled cubin is also written there and
+// later processes load it instead of compiling. A file holds a magic word,
+// the length of the generated source, the source itself and the cubin; it
+// is used only when its source equals the one wanted, so a hash collision
+// cannot load a wrong kernel. The file name hashes the source with the NVRTC
+// version and the target, so a new compiler or header never reuses an old
+// file. Files are written to a temporary name and renamed into place.
+constexpr char kCacheMagic[8] = {'M', 'L', 'K', 'B', 'C', 'U', 'B', '1'};
+
+std::string cachePath(const std::string& src) {
+    const char* dir = std::getenv("MLKB_CACHE_DIR");
+    if (dir == nullptr || dir[0] == '\0') return std::string();
+    int major = 0, minor = 0;
+    nvrtc().version(&major, &minor);
+    const std::string key = src + "|sm_100a|nvrtc" + std::to_string(major) + "." +
+                            std::to_string(minor);
+    uint64_t h = 1469598103934665603ull;  // FNV-1a, 64 bit
+    for (unsigned char ch : key) {
+        h ^= ch;
+        h *= 1099511628211ull;
+    }
+    char name[64];
+    std::snprintf(name, sizeof name, "/mlkb-chain-%016llx.cubin",
+                  static_cast<unsigned long long>(h));
+    return std::string(dir) + name;
+}
+
+bool loadCached(const std::string& path, const std::string& src, std::vector<char>& cubin) {
+    FILE* f = std::fopen(path.c_str(), "rb");
+    if (f == nullptr) return false;
+    char magic[8];
+    uint64_t len = 0;
+    bool ok = std::fread(magic, 1, 8, f) == 8 && std::memcmp(magic, kCacheMagic, 8) == 0 &&
+              std::fread(&len, sizeof len, 1, f) == 1 && len == src.size();
+    if (ok) {
+        std::string stored(len, '\0');
+        ok = std::fread(&stored[0], 1, len, f) == len && stored == src;
+    }
+    if (ok) {
+        std::vector<char> bin;
+        char buf[65536];
+        size_t got;
+        while ((got = std::fread(buf, 1, sizeof buf, f)) > 0) bin.insert(bin.end(), buf, buf + got);
+        ok = !bin.empty();
+        if (ok) cubin.swap(bin);
+    }
+    std::fclose(f);
+    return ok;
+}
+
+void storeCached(const std::string& path, const std::string& src, const std::vector<char>& cubin) {
+    const std::string dir = path.substr(0, path.rfind('/'));
+    ::mkdir(dir.c_str(), 0755);  // one level; an existing directory is fine
+    const std::string tmp = path + ".tmp." + std::to_string(::getpid());
+    FILE* f = std::fopen(tmp.c_str(), "wb");
+    if (f == nullptr) return;
+    const uint64_t len = src.size();
+    const bool ok = std::fwrite(kCacheMagic, 1, 8, f) == 8 &&
+                    std::fwrite(&len, sizeof len, 1, f) == 1 &&
+                    std::fwrite(src.data(), 1, src.size(), f) == src.size() &&
+                    std::fwrite(cubin.data(), 1, cubin.size(), f) == cubin.size();
+    if (std::fclose(f) == 0 && ok) {
+        std::rename(tmp.c_str(), path.c_str());
+    } else {
+        std::remove(tmp.c_str());
+    }
+}
+
 void compileInto(const std::string& src, Compiled& c) {
     const NvrtcApi& api = nvrtc();
+    const std::string cached = cachePath(src);
+    if (!cached.empty() && loadCached(cached, src, c.cubin)) return;
     nvrtcProgram prog = nullptr;
     const char* hdrs[1] = {kChainMathSrc};
     const char* names[1] = {"mlkb_chain_math.cuh"};
@@ -341,6 +418,7 @@ void compileInto(const std::string& src, Compiled& c) {
             c.error = "chain compile produced no cubin";
         } else {
             ++g_compiled;
+            if (!cached.empty()) storeCached(cached, src, c.cubin);
         }
     }
     api.destroy(&prog);

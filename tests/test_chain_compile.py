@@ -112,3 +112,37 @@ def test_roots_that_cannot_share_a_kernel():
         node["end"] = 100
     m = api.Module(mod)
     assert m.plan([mb.F32] * m.num_buffers) == "map_chain,map_chain"
+
+
+def test_disk_cache_serves_a_later_process(tmp_path):
+    # MLKB_CACHE_DIR: the first process compiles and stores the cubin, a later
+    # one loads it without compiling; a file whose stored source differs from
+    # the one wanted (a damaged file, or a hash collision) is not used.
+    import os
+    import subprocess
+    import sys
+
+    _nvrtc_or_skip()
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("from mlk2_b200 import api, kir\n"
+            "ch = kir.chain(kir.E('mul', kir.A, kir.C(0.3)), kir.E('tanh', kir.T(0)))\n"
+            "api.chain_build(ch, dtype='f64')\n"
+            "print(api.chain_compile(-1)[1])\n")
+    cache = tmp_path / "cache"
+    env = dict(os.environ, MLKB_CACHE_DIR=str(cache))
+
+    def compiled_in_new_process():
+        r = subprocess.run([sys.executable, "-c", code], env=env, cwd=root,
+                           capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        return int(r.stdout.strip().splitlines()[-1])
+
+    assert compiled_in_new_process() == 1
+    files = list(cache.glob("mlkb-chain-*.cubin"))
+    assert len(files) == 1 and files[0].stat().st_size > 1000
+    assert compiled_in_new_process() == 0            # loaded from the file
+    data = bytearray(files[0].read_bytes())
+    data[20] ^= 0xFF                                  # inside the stored source
+    files[0].write_bytes(bytes(data))
+    assert compiled_in_new_process() == 1            # not trusted: compiled again
+    assert compiled_in_new_process() == 0            # and the rewritten file serves

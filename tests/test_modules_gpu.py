@@ -261,3 +261,33 @@ def test_f32_chain_cancelling_after_sin_and_cos(cuda, chain_path):
         api.map_chain(ch, x, y)
         (want,) = oracle.port().chain([ch], xh.astype(np.float64))
         assert oracle.ulp_f32(host(y), want).max() <= 2, op
+
+
+def test_chain_loaded_from_the_disk_cache_runs(cuda, tmp_path):
+    # two processes with the same MLKB_CACHE_DIR: the first compiles, the
+    # second loads the stored cubin; both run the chain to the same bits
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import sys, numpy as np, torch\n"
+            "from mlk2_b200 import api, kir\n"
+            "ch = kir.chain(kir.E('mul', kir.A, kir.C(0.3)), kir.E('cos', kir.T(0)),\n"
+            "               kir.E('add', kir.T(1), kir.A))\n"
+            "x = torch.linspace(-50, 50, 100003, device='cuda')\n"
+            "y = torch.empty_like(x)\n"
+            "api.map_chain(ch, x, y)\n"
+            "np.save(sys.argv[1], y.cpu().numpy())\n"
+            "print(api.chain_compile(-1)[1])\n")
+    env = dict(os.environ, MLKB_CACHE_DIR=str(tmp_path / "cache"))
+    outs, compiled = [], []
+    for i in range(2):
+        path = str(tmp_path / f"y{i}.npy")
+        r = subprocess.run([sys.executable, "-c", code, path], env=env, cwd=root,
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+        compiled.append(int(r.stdout.strip().splitlines()[-1]))
+        outs.append(np.load(path))
+    assert compiled == [1, 0]
+    assert np.array_equal(outs[0].view(np.int32), outs[1].view(np.int32))

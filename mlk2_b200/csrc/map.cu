@@ -10,9 +10,11 @@
 //     forms it (x*x and 3x are exact in f64 for f32 x, so one FMA reproduces
 //     the Add's single rounding), sin/cos of u in f64, one final rounding to
 //     f32. HBM-bound: 8 B (map) or 12 B (map + derivative) per element.
-//   * a generic chain interpreter for any chain of scalar-realisable ops
-//     (register-slot form for chains with at most 8 temps alive at once and
-//     16-byte aligned buffers, a local-array form otherwise),
+//   * mlkb_map_chain for any chain of scalar-realisable ops: a kernel
+//     compiled at run time for the chain (chain_jit.cpp) when NVRTC is
+//     available, else the chain interpreter here (register-slot form for
+//     chains with at most 8 temps alive at once and 16-byte aligned buffers,
+//     a local-array form otherwise); both use chain_math.cuh's apply<>,
 //     f32 or f64 buffers, with the reference's guarded semantics
 //     (Div by 0 -> 0, Log of <= 0 -> 0, Sqrt of < 0 -> 0, Rsqrt of <= 0 -> 0,
 //     Pow(2,2) -> a*a). Add/Sub/Mul/Div use round-to-nearest intrinsics so

@@ -6,9 +6,13 @@
 // launch, D2H, cudaFree on every call) with:
 //   * a persistent per-device buffer cache (no allocation once warm),
 //   * one stream per device and contiguous shards over all devices,
-//   * chunked copy/compute overlap for streaming maps,
+//   * chunked copy/compute overlap for streaming maps, and pageable host
+//     buffers staged through pinned memory by a pool of host threads,
+//   * outputs assembled on device 0 by the shard kernels' own peer stores
+//     (or NCCL where a kind reads its output back),
 //   * the module bound once from its wire format instead of baked into
-//     generated source.
+//     generated source; its generic chains compiled at run time
+//     (chain_jit.cpp), roots over the same inputs into one kernel.
 #include <dlfcn.h>
 #include <nccl.h>
 

@@ -146,3 +146,28 @@ def test_disk_cache_serves_a_later_process(tmp_path):
     files[0].write_bytes(bytes(data))
     assert compiled_in_new_process() == 1            # not trusted: compiled again
     assert compiled_in_new_process() == 0            # and the rewritten file serves
+
+
+def test_without_nvrtc_chains_are_not_compiled(tmp_path):
+    # a process whose NVRTC cannot be loaded: compilation reports inactive,
+    # building a chain is refused with the reason, nothing crashes
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import mlk2_b200 as mb\n"
+            "from mlk2_b200 import api, kir\n"
+            "print(api.chain_compile(-1)[0])\n"
+            "try:\n"
+            "    api.chain_build(kir.chain(kir.E('mul', kir.A, kir.A)))\n"
+            "    print('built')\n"
+            "except mb.MLKBError as e:\n"
+            "    print('refused', e.status, 'NVRTC' in str(e))\n")
+    env = dict(os.environ, MLKB_NVRTC_LIB=str(tmp_path / "libnvrtc-missing.so"))
+    r = subprocess.run([sys.executable, "-c", code], env=env, cwd=root, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = r.stdout.strip().splitlines()
+    assert lines[-2] == "False"
+    assert lines[-1] == f"refused {mb.ERR_UNSUPPORTED} True", lines

@@ -291,3 +291,38 @@ def test_chain_loaded_from_the_disk_cache_runs(cuda, tmp_path):
         outs.append(np.load(path))
     assert compiled == [1, 0]
     assert np.array_equal(outs[0].view(np.int32), outs[1].view(np.int32))
+
+
+def test_process_without_nvrtc_gives_the_same_bits(cuda, tmp_path):
+    # the same module and inputs in a process that can load NVRTC (compiled
+    # chains, one kernel for the root group) and in one that cannot (the
+    # interpreter, root by root): identical outputs
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import sys, numpy as np, torch\n"
+            "import mlk2_b200 as mb\n"
+            "from mlk2_b200 import api, kir\n"
+            "E, A, C, T = kir.E, kir.A, kir.C, kir.T\n"
+            "chains = [kir.SIN_CHAIN, kir.DSIN_CHAIN, kir.chain(E('exp', A), E('mul', T(0), C(0.5)))]\n"
+            "m = api.Module(kir.map_module(chains, poly7=True))\n"
+            "x = torch.linspace(-9, 9, 65537, device='cuda')\n"
+            "ys = [torch.empty_like(x) for _ in chains]\n"
+            "m.run_dev([x] + ys, n=x.numel())\n"
+            "np.save(sys.argv[1], torch.stack(ys).cpu().numpy())\n"
+            "print(api.chain_compile(-1)[0], m.plan([mb.F32] * 4))\n")
+    outs, info = [], []
+    for i, lib in enumerate((None, str(tmp_path / "libnvrtc-missing.so"))):
+        env = dict(os.environ)
+        if lib is not None:
+            env["MLKB_NVRTC_LIB"] = lib
+        path = str(tmp_path / f"y{i}.npy")
+        r = subprocess.run([sys.executable, "-c", code, path], env=env, cwd=root,
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+        info.append(r.stdout.strip().splitlines()[-1])
+        outs.append(np.load(path))
+    assert info == ["True map_chains3", "False map_chains3"]
+    assert np.array_equal(outs[0].view(np.int32), outs[1].view(np.int32))

@@ -469,15 +469,17 @@ int launchChainsJit(const JitExpr* const* chains, const int* n_exprs, const bool
     {
         std::lock_guard<std::mutex> lk(g_cacheMu);
         if (c->lib == nullptr) {
+            // A cubin the driver will not load (a damaged cache file, say) is
+            // not an error for the caller: the entry is marked unusable and
+            // the chain runs on the interpreter.
             cudaError_t le = cudaLibraryLoadData(&c->lib, c->cubin.data(), nullptr, nullptr, 0,
                                                  nullptr, nullptr, 0);
+            if (le == cudaSuccess) le = cudaLibraryGetKernel(&c->kernel, c->lib, "mlkb_chain_kernel");
             if (le != cudaSuccess) {
+                cudaGetLastError();
                 c->lib = nullptr;
-                return setCudaError(MLKB_ERR_LAUNCH, le, "loading a compiled chain");
-            }
-            le = cudaLibraryGetKernel(&c->kernel, c->lib, "mlkb_chain_kernel");
-            if (le != cudaSuccess) {
-                return setCudaError(MLKB_ERR_LAUNCH, le, "compiled chain kernel lookup");
+                c->error = std::string("compiled chain not loadable: ") + cudaGetErrorString(le);
+                return kJitUnavailable;
             }
         }
         per = dev >= 0 && dev < 64 ? c->blocksPerSm[dev] : 0;

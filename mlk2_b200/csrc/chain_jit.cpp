@@ -462,12 +462,12 @@ int launchChainsJit(const JitExpr* const* chains, const int* n_exprs, const bool
     }
     Compiled* c = known.c;
     if ((known.usesA && a == nullptr) || (known.usesB && b == nullptr)) return kJitUnavailable;
-    if (!c->error.empty()) return kJitUnavailable;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
     int per = 0;
     {
-        std::lock_guard<std::mutex> lk(g_cacheMu);
+        std::lock_guard<std::mutex> lk(g_cacheMu);  // c->error, c->lib and the occupancy cache
+        if (!c->error.empty()) return kJitUnavailable;
         if (c->lib == nullptr) {
             // A cubin the driver will not load (a damaged cache file, say) is
             // not an error for the caller: the entry is marked unusable and
@@ -549,8 +549,9 @@ int buildChainJit(const JitExpr* e, int n_exprs, bool poly7, int dtype, const ch
     const bool p7[1] = {poly7};
     Generated g = generate(chains, ns, p7, 1, dtype == MLKB_F64);
     const Compiled* c = entryFor(g.src);  // entries live as long as the process
+    std::lock_guard<std::mutex> lk(g_cacheMu);
     if (!c->error.empty()) {
-        if (why) *why = c->error.c_str();
+        if (why) *why = c->error.c_str();  // set once, never changed afterwards
         return kJitUnavailable;
     }
     return MLKB_OK;

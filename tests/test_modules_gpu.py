@@ -326,3 +326,27 @@ def test_process_without_nvrtc_gives_the_same_bits(cuda, tmp_path):
         outs.append(np.load(path))
     assert info == ["True map_chains3", "False map_chains3"]
     assert np.array_equal(outs[0].view(np.int32), outs[1].view(np.int32))
+
+
+def test_root_group_with_a_large_constant_block(cuda):
+    # 8 roots x 40 expressions with 80 distinct constants each: 640 constants
+    # (5 KB) in one kernel's parameter block; each output as its root alone
+    E, A, C, T = kir.E, kir.A, kir.C, kir.T
+    chains = []
+    for r in range(8):
+        ex = [E("mul", A, C(1.0 + r / 8))]
+        for k in range(39):
+            op = "add" if k % 2 == 0 else "mul"
+            ex.append(E(op, T(len(ex) - 1), C(0.5 + 0.01 * (r * 40 + k))))
+        chains.append(kir.chain(*ex))
+    m = api.Module(kir.map_module(chains, dtype="f64"))
+    assert m.plan([mb.F64] * m.num_buffers) == "map_chains8"
+    n = 10007
+    x = dev(cuda, np.linspace(-1.0, 1.0, n))
+    outs = [empty(cuda, (n,), cuda.float64) for _ in chains]
+    api.chain_compile(1)
+    m.run_dev([x] + outs, n=n)
+    for ch, o in zip(chains, outs):
+        want = empty(cuda, (n,), cuda.float64)
+        api.map_chain(ch, x, want)
+        assert same_bits(host(o), host(want))

@@ -51,6 +51,11 @@ sys.path.insert(0, ROOT)
 
 SEED = 0x4D4C4B2B
 BYTES_PER_ELEM_MAP2 = 12  # x read + y, dy written (f32)
+# A burst starts from an idle GPU; its warm-up lasts at least this long as well
+# as W steps, so a kernel of a few microseconds (config 1: ~23 us) is not timed
+# while the GPU is still leaving its idle state. 10 ms is far below the tens of
+# milliseconds a full-power kernel runs before the power limit engages.
+BURST_WARM_S = 0.010
 
 
 def load_peaks():
@@ -573,7 +578,8 @@ def strong_configs(torch, api, mdist, args, dist, world, rank, peaks):
 
     def rec(name, fn, work, unit, peak):
         time.sleep(1.0)  # from an idle GPU, like the weak-scaling configs (a burst)
-        sec = time_device(torch, fn, args.warmup, args.steps, dist, world)
+        sec = time_device(torch, fn, args.warmup, args.steps, dist, world,
+                          min_warm_s=BURST_WARM_S)
         scale = 1e9 if unit == "GB/s" else 1e12
         out[name] = {"value": work / sec / scale, "unit": unit, "ms": sec * 1e3,
                      "frac": work / sec / scale / (world * peak), "gpu_launches": args.steps}
@@ -706,11 +712,13 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
     def measure(fn):
         """Seconds per step of a burst: each config starts from an idle GPU (1 s
         pause), so its number does not depend on the heat the previous config
-        left under the 1 kW power limit; then the same steps once more after
+        left under the 1 kW power limit, and warms up for at least W steps and
+        BURST_WARM_S; then the same steps once more after
         --min-warm-s (default 1.5 s) of continuous running, reported beside it
         as `sustained` (skipped with --min-warm-s 0)."""
         time.sleep(1.0)
-        sec = time_device(torch, fn, warm, steps, dist, world, stats=last)
+        sec = time_device(torch, fn, warm, steps, dist, world, min_warm_s=BURST_WARM_S,
+                          stats=last)
         if args.min_warm_s > 0:
             sus = time_device(torch, fn, 0, steps, dist, world, min_warm_s=args.min_warm_s)
             last["sustained_ms_per_step"] = sus * 1e3

@@ -55,6 +55,7 @@ BYTES_PER_ELEM_MAP2 = 12  # x read + y, dy written (f32)
 # as W steps, so a kernel of a few microseconds (config 1: ~23 us) is not timed
 # while the GPU is still leaving its idle state. 10 ms is far below the tens of
 # milliseconds a full-power kernel runs before the power limit engages.
+# --min-warm-s 0 (profiling runs) drops it with the other time-based warm-ups.
 BURST_WARM_S = 0.010
 
 
@@ -356,7 +357,8 @@ def main():
     ap.add_argument("--headline-only", action="store_true")
     ap.add_argument("--min-warm-s", type=float, default=1.5,
                     help="headline warm-up continues at least this long (clock samples); "
-                         "also the run-in of each config's sustained figure (0: none)")
+                         "also the run-in of each config's sustained figure; 0: neither, "
+                         "and bursts warm up for W steps only (profiling runs)")
     ap.add_argument("--case", default=None,
                     choices=["map1", "map2", "chain", "softmax", "gemm", "gemm_f32", "qk", "qk_kt"],
                     help="run one kernel W+K times (profiling target), no JSON line")
@@ -579,7 +581,7 @@ def strong_configs(torch, api, mdist, args, dist, world, rank, peaks):
     def rec(name, fn, work, unit, peak):
         time.sleep(1.0)  # from an idle GPU, like the weak-scaling configs (a burst)
         sec = time_device(torch, fn, args.warmup, args.steps, dist, world,
-                          min_warm_s=BURST_WARM_S)
+                          min_warm_s=BURST_WARM_S if args.min_warm_s > 0 else 0.0)
         scale = 1e9 if unit == "GB/s" else 1e12
         out[name] = {"value": work / sec / scale, "unit": unit, "ms": sec * 1e3,
                      "frac": work / sec / scale / (world * peak), "gpu_launches": args.steps}
@@ -717,8 +719,8 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
         --min-warm-s (default 1.5 s) of continuous running, reported beside it
         as `sustained` (skipped with --min-warm-s 0)."""
         time.sleep(1.0)
-        sec = time_device(torch, fn, warm, steps, dist, world, min_warm_s=BURST_WARM_S,
-                          stats=last)
+        sec = time_device(torch, fn, warm, steps, dist, world,
+                          min_warm_s=BURST_WARM_S if args.min_warm_s > 0 else 0.0, stats=last)
         if args.min_warm_s > 0:
             sus = time_device(torch, fn, 0, steps, dist, world, min_warm_s=args.min_warm_s)
             last["sustained_ms_per_step"] = sus * 1e3

@@ -771,7 +771,7 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
          "parity": g1})
     del xs1, ys1
 
-    # the generic chain path: the derivative chain the
+    # the generic chain path (every scalar-realisable chain): the derivative chain the
     # reference's calculus passes emit for config 2 (Tier-1 output committed in
     # tests/golden/pipeline.npz), 2^28 f32 through mlkb_map_chain, which runs
     # it as a chain kernel compiled at run time (no dedicated kernel applies

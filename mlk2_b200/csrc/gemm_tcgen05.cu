@@ -293,6 +293,12 @@ gemm_f16_tcgen05_pair(const __grid_constant__ CUtensorMap tma_a,
     __syncthreads();
     tc::cluster_sync();  // barriers of both CTAs initialised before any remote use
     tc::tc_fence_after();
+    // Programmatic dependent launch: the set-up above overlaps the tail of the
+    // preceding grid; wait for it (its writes visible: C may be accumulated
+    // into) before any global access, and let the next grid be scheduled as
+    // our CTAs retire. Both are no-ops for a plain launch.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t tmem = s.tmem_base;
     volatile int* abort = &s.abort;
 
@@ -536,9 +542,22 @@ int launchGemmPair(const void* a, const void* b, float* c, int64_t m, int64_t n,
     const int64_t tiles = ((m + 2 * kBM - 1) / (2 * kBM)) * ((n + kBN - 1) / kBN);
     const int64_t pairs_max = smCount() / 2;
     const int grid = 2 * static_cast<int>(tiles < pairs_max ? tiles : pairs_max);
-    gemm_f16_tcgen05_pair<<<grid, kThreads, kPairSmemBytes, s>>>(
-        ta, tb, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), accumulate,
-        deviceStatusPtr());
+    // Programmatic stream serialization (the kernel waits for its predecessor
+    // itself); the cluster shape comes from the kernel's __cluster_dims__.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kPairSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_f16_tcgen05_pair, ta, tb, c,
+                                              static_cast<int>(m), static_cast<int>(n),
+                                              static_cast<int>(k), accumulate, deviceStatusPtr());
+    if (le != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, le, "gemm tcgen05 pair launch");
     return checkLaunch("gemm tcgen05 pair launch");
 }
 

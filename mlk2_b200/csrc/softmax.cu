@@ -126,6 +126,12 @@ softmax_rows_tma(const float* __restrict__ x, float* __restrict__ y, int64_t row
     }
     tab[tid] = exp2(static_cast<double>(tid) * (1.0 / 256.0));  // kRowThreads == 256
     __syncthreads();
+    // Programmatic dependent launch: the set-up above overlaps the tail of
+    // the preceding grid in the stream; wait for it to finish (its writes
+    // visible) before touching global memory, and let the next grid's CTAs
+    // be scheduled as ours retire. Both are no-ops for a plain launch.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (tid == 0) {
         for (int b = 0; b < 2; ++b) {
             const int64_t r = blockIdx.x + static_cast<int64_t>(b) * gridDim.x;
@@ -385,8 +391,21 @@ int launchRowsTma(const float* x, float* y, int64_t rows, int64_t cols, cudaStre
     // hardware rebalances the short CTAs across SMs (6 % faster than one
     // resident wave of persistent CTAs).
     const int per_sm = 4 * (NV <= 2 ? 8 : NV <= 4 ? 6 : 3);
-    softmax_rows_tma<NV, kFull><<<rowGrid(rows, per_sm), kRowThreads, smem, s>>>(
-        x, y, rows, cols, deviceStatusPtr());
+    // Launched with programmatic stream serialization (the kernel waits for
+    // its predecessor itself): back-to-back launches overlap launch and tail.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rowGrid(rows, per_sm));
+    cfg.blockDim = dim3(kRowThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, softmax_rows_tma<NV, kFull>, x, y, rows, cols,
+                                              deviceStatusPtr());
+    if (le != cudaSuccess) return setCudaError(MLKB_ERR_LAUNCH, le, "softmax launch");
     return checkLaunch("softmax launch");
 }
 

@@ -25,7 +25,9 @@ of y and dy inside every one of the K steps.
 With N > 1 ranks a strong-scaling pass follows: each fixed BASELINE problem
 (2^24 / 2^28 elements, 65536 rows, M = 8192, 256 batches) is split over the
 N ranks and timed the same way, plus the NCCL all-gather that assembles the
-config-2 result.
+config-2 result. Config 1's shard (a few microseconds of kernel at N = 8) is
+timed as one CUDA graph of the K steps over input/output pairs rotated past
+twice the L2's size, since an eager loop would time the host's launch cost.
 
 The line is kept short (the full record goes to --detail PATH): the driver
 keeps the end of stdout, so `configs` and `strong` come last, in short keys:

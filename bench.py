@@ -573,6 +573,16 @@ def main():
         dist.destroy_process_group()
 
 
+def rotation_pairs(pair_bytes, steps, l2_bytes):
+    """How many input/output pairs a rotating config-1 loop uses: the smallest
+    count d that divides K (so the rotation also holds across replays of a
+    graph of the K steps) and puts at least twice the L2's size of other
+    pairs' traffic, (d - 1) * pair_bytes, between two uses of one pair; K when
+    no divisor does."""
+    need = -(-2 * l2_bytes // pair_bytes) + 1
+    return next((d for d in range(max(need, 1), steps + 1) if steps % d == 0), steps)
+
+
 def graph_of_steps(torch, fn, steps):
     """`steps` calls of fn captured into one CUDA graph on a side stream (fn
     launches on the current stream, which the capture makes the side one)."""
@@ -620,14 +630,10 @@ def strong_configs(torch, api, mdist, args, dist, world, rank, peaks):
         return total * (rank + 1) // world - total * rank // world
 
     # config 1 (2^24) and config 2 (2^28) element shards. A config-1 shard is
-    # 16-128 MB, so steps rotate over `pairs` input/output pairs: each step's
-    # pair was last touched more than twice the L2's size of traffic earlier.
-    # `pairs` divides K, so this holds across graph replays too.
+    # 16-128 MB, so steps rotate over input/output pairs (rotation_pairs).
     n1 = part(1 << 24)
     l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
-    need = -(-2 * l2 // (n1 * 8))
-    pairs = next((d for d in range(max(need, 1), args.steps + 1) if args.steps % d == 0),
-                 args.steps)
+    pairs = rotation_pairs(n1 * 8, args.steps, l2)
     x1s = [torch.empty(n1, device="cuda") for _ in range(pairs)]
     y1s = [torch.empty_like(x1s[0]) for _ in range(pairs)]
     for x in x1s:
@@ -764,8 +770,8 @@ def other_configs(torch, api, args, dist, world, rank, peaks, traffic):
         --min-warm-s (default 1.5 s) of continuous running, reported beside it
         as `sustained` (skipped with --min-warm-s 0)."""
         time.sleep(1.0)
-        sec = time_device(torch, fn, warm, steps, dist, world,
-                          min_warm_s=BURST_WARM_S if args.min_warm_s > 0 else 0.0, stats=last)
+        warm_s = BURST_WARM_S if args.min_warm_s > 0 else 0.0
+        sec = time_device(torch, fn, warm, steps, dist, world, min_warm_s=warm_s, stats=last)
         if args.min_warm_s > 0:
             sus = time_device(torch, fn, 0, steps, dist, world, min_warm_s=args.min_warm_s)
             last["sustained_ms_per_step"] = sus * 1e3
